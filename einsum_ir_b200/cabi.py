@@ -1,0 +1,237 @@
+"""ctypes binding of the C-ABI declared in include/eir_cuda.h.
+
+The library is loaded from this package directory (built in-tree by
+``einsum_ir_b200.build``). There is no fallback: if the shared library is
+missing or cannot be loaded, every entry point raises.
+"""
+from __future__ import annotations
+
+import ctypes
+from ctypes import POINTER, c_char_p, c_int32, c_int64, c_void_p
+from pathlib import Path
+from typing import Iterable, Sequence
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libeinsum_ir_b200.so"
+
+# ---- enums (values of include/eir_cuda.h)
+SUCCESS = 0
+DIM_C, DIM_M, DIM_N, DIM_K = 0, 1, 2, 3
+FP32, FP64, BF16 = 0, 1, 2
+COMPUTE_DEFAULT, COMPUTE_FP32, COMPUTE_TF32, COMPUTE_FP64, COMPUTE_BF16 = 0, 1, 2, 3, 4
+KTYPE_ZERO, KTYPE_RELU, KTYPE_ADD, KTYPE_COPY, KTYPE_MADD, KTYPE_UNDEFINED = 0, 1, 2, 3, 4, 99
+FAMILY_NONE, FAMILY_SIMT, FAMILY_TC, FAMILY_PERMUTE, FAMILY_DMMA = 0, 1, 2, 3, 4
+FLAG_FORCE_SIMT, FLAG_NO_PREPACK = 1, 2
+
+# every symbol include/eir_cuda.h declares (checked by the CPU test suite)
+EXPORTS = [
+    "eir_contract_plan_create", "eir_contract", "eir_contract_num_ops",
+    "eir_permute_plan_create", "eir_permute", "eir_plan_destroy", "eir_plan_kernel_family",
+    "eir_plan_workspace_bytes", "eir_plan_describe", "eir_expression_create",
+    "eir_expression_eval", "eir_expression_num_ops", "eir_expression_num_tensors",
+    "eir_expression_tensor_dims", "eir_expression_destroy", "eir_expression_describe",
+    "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
+]
+
+
+class EirDim(ctypes.Structure):
+    _fields_ = [("type", c_int32), ("pad_", c_int32), ("size", c_int64),
+                ("stride_left", c_int64), ("stride_right", c_int64),
+                ("stride_out", c_int64), ("stride_out_aux", c_int64)]
+
+
+class EirContractDesc(ctypes.Structure):
+    _fields_ = [("num_dims", c_int32), ("dtype_left", c_int32), ("dtype_right", c_int32),
+                ("dtype_out", c_int32), ("dtype_comp", c_int32),
+                ("ktype_first_touch", c_int32), ("ktype_main", c_int32),
+                ("ktype_last_touch", c_int32), ("flags", c_int32), ("pad_", c_int32),
+                ("dims", POINTER(EirDim))]
+
+
+class EirError(RuntimeError):
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"einsum_ir_b200 error {code}: {msg}")
+        self.code = code
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    """Load the shared library once (raises if it is missing)."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise EirError(-1, f"{LIB_PATH} missing: run einsum_ir_b200.build.build()")
+        L = ctypes.CDLL(str(LIB_PATH))
+        L.eir_contract_plan_create.argtypes = [POINTER(EirContractDesc), POINTER(c_void_p)]
+        L.eir_contract.argtypes = [c_void_p] * 6
+        L.eir_contract_num_ops.argtypes = [c_void_p]
+        L.eir_contract_num_ops.restype = c_int64
+        L.eir_permute_plan_create.argtypes = [c_int32, POINTER(c_int64), POINTER(c_int64),
+                                              POINTER(c_int64), c_int32, POINTER(c_void_p)]
+        L.eir_permute.argtypes = [c_void_p] * 4
+        L.eir_plan_destroy.argtypes = [c_void_p]
+        L.eir_plan_kernel_family.argtypes = [c_void_p]
+        L.eir_plan_workspace_bytes.argtypes = [c_void_p]
+        L.eir_plan_workspace_bytes.restype = c_int64
+        L.eir_plan_describe.argtypes = [c_void_p]
+        L.eir_plan_describe.restype = c_char_p
+        L.eir_last_error_string.restype = c_char_p
+        L.eir_check_device_errors.argtypes = [c_void_p]
+        L.eir_launch_count.restype = c_int64
+        if hasattr(L, "eir_expression_create"):
+            L.eir_expression_create.argtypes = [c_char_p, c_char_p, c_char_p, c_int32, c_int32,
+                                                 POINTER(c_void_p)]
+            L.eir_expression_eval.argtypes = [c_void_p, POINTER(c_void_p), c_void_p]
+            L.eir_expression_num_ops.argtypes = [c_void_p]
+            L.eir_expression_num_ops.restype = c_int64
+            L.eir_expression_num_tensors.argtypes = [c_void_p]
+            L.eir_expression_tensor_dims.argtypes = [c_void_p, c_int32, POINTER(c_int64), c_int32]
+            L.eir_expression_destroy.argtypes = [c_void_p]
+            L.eir_expression_describe.argtypes = [c_void_p]
+            L.eir_expression_describe.restype = c_char_p
+        _lib = L
+    return _lib
+
+
+def check(rc: int) -> None:
+    if rc != SUCCESS:
+        raise EirError(rc, lib().eir_last_error_string().decode())
+
+
+def launch_count() -> int:
+    return int(lib().eir_launch_count())
+
+
+def check_device_errors(stream: int = 0) -> None:
+    check(lib().eir_check_device_errors(c_void_p(stream)))
+
+
+def _ptr(x) -> c_void_p:
+    if x is None:
+        return c_void_p(None)
+    if isinstance(x, int):
+        return c_void_p(x)
+    if hasattr(x, "data_ptr"):
+        return c_void_p(x.data_ptr())
+    raise TypeError(f"cannot take a device pointer of {type(x)}")
+
+
+class Plan:
+    def __init__(self, handle: c_void_p):
+        self._h = handle
+
+    @property
+    def handle(self) -> c_void_p:
+        return self._h
+
+    @property
+    def family(self) -> int:
+        return int(lib().eir_plan_kernel_family(self._h))
+
+    @property
+    def workspace_bytes(self) -> int:
+        return int(lib().eir_plan_workspace_bytes(self._h))
+
+    def describe(self) -> str:
+        return lib().eir_plan_describe(self._h).decode()
+
+    def close(self) -> None:
+        if self._h:
+            lib().eir_plan_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class ContractPlan(Plan):
+    """A compiled strided binary contraction (eir_contract_plan_create)."""
+
+    def __init__(self, dims: Sequence[tuple], dtype_left: int, dtype_right: int, dtype_out: int,
+                 dtype_comp: int = COMPUTE_DEFAULT, first: int = KTYPE_ZERO,
+                 main: int = KTYPE_MADD, last: int = KTYPE_UNDEFINED, flags: int = 0):
+        arr = (EirDim * max(1, len(dims)))()
+        for i, d in enumerate(dims):
+            t, size, sl, sr, so, sa = d
+            arr[i] = EirDim(t, 0, size, sl, sr, so, sa)
+        desc = EirContractDesc(len(dims), dtype_left, dtype_right, dtype_out, dtype_comp,
+                               first, main, last, flags, 0, arr)
+        h = c_void_p()
+        check(lib().eir_contract_plan_create(ctypes.byref(desc), ctypes.byref(h)))
+        super().__init__(h)
+        self.dims = list(dims)
+
+    @property
+    def num_ops(self) -> int:
+        return int(lib().eir_contract_num_ops(self._h))
+
+    def contract(self, left, right, out, aux=None, stream: int = 0) -> None:
+        check(lib().eir_contract(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
+                                 c_void_p(stream)))
+
+
+class PermutePlan(Plan):
+    """A compiled permute (eir_permute_plan_create)."""
+
+    def __init__(self, sizes: Sequence[int], strides_in: Sequence[int],
+                 strides_out: Sequence[int], dtype: int):
+        n = len(sizes)
+        a = (c_int64 * max(1, n))(*sizes)
+        b = (c_int64 * max(1, n))(*strides_in)
+        c = (c_int64 * max(1, n))(*strides_out)
+        h = c_void_p()
+        check(lib().eir_permute_plan_create(n, a, b, c, dtype, ctypes.byref(h)))
+        super().__init__(h)
+
+    def permute(self, src, dst, stream: int = 0) -> None:
+        check(lib().eir_permute(self._h, _ptr(src), _ptr(dst), c_void_p(stream)))
+
+
+class Expression:
+    """An einsum expression compiled into a tree of contractions (eir_expression_*)."""
+
+    def __init__(self, expr: str, sizes: str, path: str, dtype: int = FP32,
+                 dtype_comp: int = COMPUTE_DEFAULT):
+        h = c_void_p()
+        check(lib().eir_expression_create(expr.encode(), sizes.encode(), path.encode(), dtype,
+                                          dtype_comp, ctypes.byref(h)))
+        self._h = h
+
+    @property
+    def num_ops(self) -> int:
+        return int(lib().eir_expression_num_ops(self._h))
+
+    @property
+    def num_tensors(self) -> int:
+        return int(lib().eir_expression_num_tensors(self._h))
+
+    def tensor_shape(self, i: int) -> list[int]:
+        buf = (c_int64 * 64)()
+        n = lib().eir_expression_tensor_dims(self._h, i, buf, 64)
+        if n < 0:
+            check(-n)
+        return [int(buf[j]) for j in range(n)]
+
+    def describe(self) -> str:
+        return lib().eir_expression_describe(self._h).decode()
+
+    def eval(self, tensors: Iterable, stream: int = 0) -> None:
+        ptrs = [(_ptr(t).value or 0) for t in tensors]
+        arr = (c_void_p * len(ptrs))(*ptrs)
+        check(lib().eir_expression_eval(self._h, arr, c_void_p(stream)))
+
+    def close(self) -> None:
+        if self._h:
+            lib().eir_expression_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass

@@ -1,0 +1,838 @@
+// C-ABI of the einsum_ir B200 backend: planning (lowering of a strided binary
+// contraction or permute to one of the kernel families) and launches.
+//
+// Lowering, in the spirit of the reference's ContractionOptimizer
+// (ContractionOptimizer.cpp:47-111: drop size-1 loops, fuse contiguous loops)
+// but with B200 targets instead of CPU GEMM leaves:
+//   1. size-1 dims are dropped; dims of one type whose strides are contiguous
+//      in every tensor are fused;
+//   2. tensor-core path (BF16, TF32, 3xTF32): choose a primitive K dim that is
+//      stride-1 in a K-major operand (or any K dim if both operands are
+//      MN-major), the primitive M / N dims (the output's fastest M dim), map
+//      the other K dims to up to two outer K loops and the other C / M / N dims
+//      to up to four tile loops, and describe each operand as a 5-D TMA map
+//      over its native strides. If both operands are K-major with different
+//      stride-1 K dims the smaller operand is pre-permuted into a workspace
+//      (the reference packs with a transpose for the same reason,
+//      ContractionOptimizer.cpp:337-447);
+//   3. otherwise the generic SIMT kernel reads the operands in place.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <algorithm>
+#include <atomic>
+#include <cstdio>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <string>
+#include <vector>
+#include "eir_kernels.h"
+#include "eir_plan.h"
+
+using eir::LDim;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<int64_t> g_launches{0};
+
+int set_error(int code, std::string const &msg) {
+  g_last_error = msg;
+  return code;
+}
+
+int cuda_fail(cudaError_t e, char const *where) {
+  return set_error(EIR_CUDA_ERROR, std::string(where) + ": " + cudaGetErrorString(e));
+}
+
+// ---- per-device state: SM count, device error word
+struct DeviceState {
+  int num_sms = 0;
+  uint32_t *err = nullptr;
+};
+std::mutex g_dev_mu;
+DeviceState g_dev[64];
+
+int device_state(DeviceState **out) {
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (dev < 0 || dev >= 64) return set_error(EIR_CUDA_ERROR, "device index out of range");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceState &d = g_dev[dev];
+  if (d.num_sms == 0) {
+    int n = 0;
+    e = cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaDeviceGetAttribute");
+    e = cudaMalloc(&d.err, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMalloc(error word)");
+    e = cudaMemset(d.err, 0, sizeof(uint32_t));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error word)");
+    d.num_sms = n;
+  }
+  *out = &d;
+  return EIR_SUCCESS;
+}
+
+// ---- driver entry point for tensor-map encoding (no link against libcuda)
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+std::once_flag g_encode_once;
+
+int get_encoder() {
+  std::call_once(g_encode_once, []() {
+    void *fn = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+  });
+  if (g_encode == nullptr) return set_error(EIR_CUDA_ERROR, "cuTensorMapEncodeTiled unavailable");
+  return EIR_SUCCESS;
+}
+
+int encode_map(eir::MapSpec const &s, void const *ptr, CUtensorMap *m) {
+  int rc = get_encoder();
+  if (rc != EIR_SUCCESS) return rc;
+  uint32_t estr[5] = {1, 1, 1, 1, 1};
+  CUresult r = g_encode(m, s.dtype, s.rank, const_cast<void *>(ptr), s.dims, s.strides_bytes, s.box,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS)
+    return set_error(EIR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
+  return EIR_SUCCESS;
+}
+
+int64_t dtype_bytes(int dt) {
+  switch (dt) {
+    case EIR_FP32: return 4;
+    case EIR_FP64: return 8;
+    case EIR_BF16: return 2;
+    default: return -1;
+  }
+}
+
+int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+char const *type_name(int t) {
+  switch (t) {
+    case EIR_DIM_C: return "C";
+    case EIR_DIM_M: return "M";
+    case EIR_DIM_N: return "N";
+    case EIR_DIM_K: return "K";
+    default: return "?";
+  }
+}
+
+// drop size-1 dims and fuse dims of one type that are contiguous in every tensor
+std::vector<LDim> simplify_dims(std::vector<LDim> d) {
+  d.erase(std::remove_if(d.begin(), d.end(), [](LDim const &x) { return x.size == 1; }), d.end());
+  bool changed = true;
+  while (changed) {
+    changed = false;
+    for (size_t i = 0; i < d.size() && !changed; ++i) {
+      for (size_t o = 0; o < d.size() && !changed; ++o) {
+        if (i == o || d[i].type != d[o].type) continue;
+        LDim const &in = d[i];
+        LDim const &ou = d[o];
+        if (ou.sl == in.sl * in.size && ou.sr == in.sr * in.size && ou.so == in.so * in.size &&
+            ou.sa == in.sa * in.size) {
+          LDim f = in;
+          f.size = in.size * ou.size;
+          d[i] = f;
+          d.erase(d.begin() + o);
+          changed = true;
+        }
+      }
+    }
+  }
+  return d;
+}
+
+int build_group(std::vector<LDim> const &dims, int type, eir::GroupDims *g) {
+  std::vector<LDim> sel;
+  for (auto const &x : dims)
+    if (x.type == type) sel.push_back(x);
+  if ((int)sel.size() > eir::kMaxGroupDims) return -1;
+  // fastest index first: order by the stride that matters for coalescing
+  std::stable_sort(sel.begin(), sel.end(), [type](LDim const &a, LDim const &b) {
+    int64_t ka = (type == EIR_DIM_K) ? std::llabs(a.sl) : std::llabs(a.so);
+    int64_t kb = (type == EIR_DIM_K) ? std::llabs(b.sl) : std::llabs(b.so);
+    return ka < kb;
+  });
+  g->n = (int)sel.size();
+  g->total = 1;
+  for (int i = 0; i < g->n; ++i) {
+    g->size[i] = sel[i].size;
+    g->sl[i] = sel[i].sl;
+    g->sr[i] = sel[i].sr;
+    g->so[i] = sel[i].so;
+    g->sa[i] = sel[i].sa;
+    g->total *= sel[i].size;
+  }
+  return 0;
+}
+
+int64_t min_abs_stride(std::vector<LDim> const &dims, int type, bool left) {
+  int64_t m = INT64_MAX;
+  for (auto const &x : dims)
+    if (x.type == type) m = std::min<int64_t>(m, std::llabs(left ? x.sl : x.sr));
+  return m;
+}
+
+int64_t env_int(char const *name, int64_t dflt) {
+  char const *v = std::getenv(name);
+  if (v == nullptr || *v == 0) return dflt;
+  return std::atoll(v);
+}
+
+// Permute planning shared by eir_permute_plan_create and operand pre-packing.
+int plan_permute(int nd, int64_t const *sizes, int64_t const *sin, int64_t const *sout, int esize,
+                 eir::PermuteParams *pp, std::string *text) {
+  std::vector<LDim> d;
+  for (int i = 0; i < nd; ++i) {
+    if (sizes[i] < 0) return set_error(EIR_INVALID_ARGUMENT, "negative permute size");
+    LDim x;
+    x.type = 0;
+    x.size = sizes[i];
+    x.sl = sin[i];
+    x.so = sout[i];
+    d.push_back(x);
+  }
+  int64_t total = 1;
+  for (auto const &x : d) total *= x.size;
+  d = simplify_dims(d);
+  *pp = eir::PermuteParams();
+  pp->total = total;
+  if (total == 0 || d.empty()) {
+    // scalar (all dims size 1) or empty tensor
+    pp->nd = 1;
+    pp->size[0] = total == 0 ? 0 : 1;
+    pp->sin[0] = 1;
+    pp->sout[0] = 1;
+    pp->rows = 1;
+    pp->mode = 0;
+    pp->vec = 1;
+    if (text) *text = "permute: scalar/empty";
+    return EIR_SUCCESS;
+  }
+  if ((int)d.size() > eir::kMaxPermDims)
+    return set_error(EIR_COMPILATION_FAILED, "permute has too many non-fusable dims");
+  // dim 0 = the output's fastest dim
+  std::stable_sort(d.begin(), d.end(),
+                   [](LDim const &a, LDim const &b) { return std::llabs(a.so) < std::llabs(b.so); });
+  int tin = 0;
+  for (int i = 1; i < (int)d.size(); ++i)
+    if (std::llabs(d[i].sl) < std::llabs(d[tin].sl)) tin = i;
+  pp->nd = (int)d.size();
+  for (int i = 0; i < pp->nd; ++i) {
+    pp->size[i] = d[i].size;
+    pp->sin[i] = d[i].sl;
+    pp->sout[i] = d[i].so;
+  }
+  if (tin == 0 || d[0].so != 1 || d[tin].sl != 1) {
+    // shared fastest dim (or no unit strides at all): row copy
+    pp->mode = 0;
+    int vec = 1;
+    if (d[0].so == 1 && d[0].sl == 1) {
+      vec = (int)(16 / esize);
+      while (vec > 1) {
+        bool ok = d[0].size % vec == 0;
+        for (int i = 1; i < pp->nd; ++i) ok = ok && (d[i].sl % vec == 0) && (d[i].so % vec == 0);
+        if (ok) break;
+        vec /= 2;
+      }
+    } else if (tin != 0) {
+      // no unit stride on one side: still correct with the generic row copy;
+      // put the dims in the row decomposition by treating dim 0 as scalar rows
+      vec = 1;
+    }
+    pp->vec = vec;
+    pp->rows = total / d[0].size;
+    if (text) *text = "permute: row copy, vec=" + std::to_string(vec) + ", nd=" + std::to_string(pp->nd);
+  } else {
+    pp->mode = 1;
+    pp->tdim_in = tin;
+    pp->batch = total / (d[0].size * d[tin].size);
+    if (text) *text = "permute: 32x32 tile transpose, nd=" + std::to_string(pp->nd);
+  }
+  return EIR_SUCCESS;
+}
+
+// ------------------------------------------------------------- TC lowering
+struct TcChoice {
+  bool ok = false;
+  int prepack = -1;                 // operand to pre-permute (0 left, 1 right)
+  std::vector<int64_t> pre_order;   // prepack: dim indices, outermost first
+};
+
+int dim_index_with_unit_stride(std::vector<LDim> const &d, int type, bool left) {
+  for (int i = 0; i < (int)d.size(); ++i)
+    if (d[i].type == type && (left ? d[i].sl : d[i].sr) == 1) return i;
+  return -1;
+}
+
+bool try_tc(eir_plan *p, std::string *why) {
+  std::vector<LDim> &d = p->dims;
+  int kind;
+  if (p->dt_l == EIR_BF16 && p->dt_r == EIR_BF16 && p->dt_o == EIR_FP32) {
+    if (p->comp != EIR_COMPUTE_DEFAULT && p->comp != EIR_COMPUTE_BF16) {
+      *why = "bf16 inputs need BF16/default compute";
+      return false;
+    }
+    kind = 0;
+  } else if (p->dt_l == EIR_FP32 && p->dt_r == EIR_FP32 && p->dt_o == EIR_FP32) {
+    kind = (p->comp == EIR_COMPUTE_TF32) ? 1 : 2;
+  } else {
+    *why = "dtype has no tensor-core path";
+    return false;
+  }
+  const int esize = kind == 0 ? 2 : 4;
+  int nc = 0, nm = 0, nn = 0, nk = 0;
+  for (auto const &x : d) {
+    if (x.size <= 0 || x.size >= (int64_t(1) << 31)) {
+      *why = "dim size out of TMA coordinate range";
+      return false;
+    }
+    if (x.type == EIR_DIM_C) ++nc;
+    if (x.type == EIR_DIM_M) ++nm;
+    if (x.type == EIR_DIM_N) ++nn;
+    if (x.type == EIR_DIM_K) ++nk;
+    bool in_l = x.type != EIR_DIM_N, in_r = x.type != EIR_DIM_M, in_o = x.type != EIR_DIM_K;
+    if ((in_l && x.sl == 0) || (in_r && x.sr == 0) || (in_o && x.so == 0)) {
+      *why = "broadcast (zero-stride) operand dim";
+      return false;
+    }
+  }
+  if (nm == 0 || nn == 0 || nk == 0) {
+    *why = "needs at least one M, N and K dim";
+    return false;
+  }
+  int64_t cmn = 1, kk = 1;
+  for (auto const &x : d) (x.type == EIR_DIM_K ? kk : cmn) *= x.size;
+  if (2.0 * (double)cmn * (double)kk < (double)env_int("EIR_TC_MIN_OPS", int64_t(1) << 24)) {
+    *why = "below tensor-core size threshold";
+    return false;
+  }
+
+  int a_k1 = dim_index_with_unit_stride(d, EIR_DIM_K, true);
+  int a_m1 = dim_index_with_unit_stride(d, EIR_DIM_M, true);
+  int b_k1 = dim_index_with_unit_stride(d, EIR_DIM_K, false);
+  int b_n1 = dim_index_with_unit_stride(d, EIR_DIM_N, false);
+  bool no_prepack = (p->desc_flags & EIR_FLAG_NO_PREPACK) != 0;
+
+  int kp = -1;
+  bool a_mn = false, b_mn = false;
+  int prepack = -1;
+  auto largest_k = [&]() {
+    int best = -1;
+    for (int i = 0; i < (int)d.size(); ++i)
+      if (d[i].type == EIR_DIM_K && (best < 0 || d[i].size > d[best].size)) best = i;
+    return best;
+  };
+  auto bytes_of = [&](bool left) {
+    int64_t n = 1;
+    for (auto const &x : d)
+      if (x.type == EIR_DIM_C || x.type == EIR_DIM_K || x.type == (left ? EIR_DIM_M : EIR_DIM_N))
+        n *= x.size;
+    return n * esize;
+  };
+  if (a_k1 >= 0 && b_k1 >= 0 && a_k1 == b_k1) {
+    kp = a_k1;
+  } else if (a_k1 >= 0 && b_n1 >= 0) {
+    kp = a_k1;
+    b_mn = true;
+  } else if (a_m1 >= 0 && b_k1 >= 0) {
+    kp = b_k1;
+    a_mn = true;
+  } else if (a_m1 >= 0 && b_n1 >= 0) {
+    kp = largest_k();
+    a_mn = b_mn = true;
+  } else if (!no_prepack && a_k1 >= 0 && b_k1 >= 0) {
+    // K-order mismatch: re-layout the smaller operand around the other's K dim
+    if (bytes_of(false) <= bytes_of(true)) {
+      prepack = 1;
+      kp = a_k1;
+    } else {
+      prepack = 0;
+      kp = b_k1;
+    }
+  } else if (!no_prepack && (a_k1 >= 0 || a_m1 >= 0) && b_k1 < 0 && b_n1 < 0) {
+    prepack = 1;
+    kp = a_k1 >= 0 ? a_k1 : largest_k();
+    a_mn = a_k1 < 0;
+  } else if (!no_prepack && (b_k1 >= 0 || b_n1 >= 0) && a_k1 < 0 && a_m1 < 0) {
+    prepack = 0;
+    kp = b_k1 >= 0 ? b_k1 : largest_k();
+    b_mn = b_k1 < 0;
+  } else {
+    *why = "no unit-stride K or row dim usable for TMA";
+    return false;
+  }
+
+  // primitive M / N
+  int mp = -1, np = -1;
+  if (a_mn) {
+    mp = a_m1;
+  } else {
+    for (int i = 0; i < (int)d.size(); ++i)
+      if (d[i].type == EIR_DIM_M &&
+          (mp < 0 || std::llabs(d[i].so) < std::llabs(d[mp].so) ||
+           (std::llabs(d[i].so) == std::llabs(d[mp].so) && d[i].size > d[mp].size)))
+        mp = i;
+  }
+  if (b_mn) {
+    np = b_n1;
+  } else {
+    for (int i = 0; i < (int)d.size(); ++i)
+      if (d[i].type == EIR_DIM_N &&
+          (np < 0 || d[i].size > d[np].size ||
+           (d[i].size == d[np].size && std::llabs(d[i].so) < std::llabs(d[np].so))))
+        np = i;
+  }
+
+  // pre-permute: packed layout of the operand with its dims in descending
+  // stride order, except the primitive K dim which becomes innermost
+  std::vector<int64_t> packed_stride(d.size(), 0);
+  if (prepack >= 0) {
+    bool left = prepack == 0;
+    std::vector<int> ids;
+    for (int i = 0; i < (int)d.size(); ++i)
+      if (d[i].type == EIR_DIM_C || d[i].type == EIR_DIM_K ||
+          d[i].type == (left ? EIR_DIM_M : EIR_DIM_N))
+        if (i != kp) ids.push_back(i);
+    std::stable_sort(ids.begin(), ids.end(), [&](int a, int b) {
+      return std::llabs(left ? d[a].sl : d[a].sr) > std::llabs(left ? d[b].sl : d[b].sr);
+    });
+    ids.push_back(kp);
+    int64_t s = 1;
+    for (int j = (int)ids.size() - 1; j >= 0; --j) {
+      packed_stride[ids[j]] = s;
+      s *= d[ids[j]].size;
+    }
+    // if the packed operand is MN-major (other operand MN-major, kp innermost) it is K-major now
+    if (left) a_mn = false;
+    else b_mn = false;
+  }
+  auto sl_of = [&](int i) { return prepack == 0 ? packed_stride[i] : d[i].sl; };
+  auto sr_of = [&](int i) { return prepack == 1 ? packed_stride[i] : d[i].sr; };
+
+  // outer K dims and tile loops
+  std::vector<int> ko, loops;
+  for (int i = 0; i < (int)d.size(); ++i) {
+    if (i == kp || i == mp || i == np) continue;
+    if (d[i].type == EIR_DIM_K) ko.push_back(i);
+    else loops.push_back(i);
+  }
+  if (ko.size() > 2) {
+    *why = "more than two outer K dims";
+    return false;
+  }
+  if ((int)loops.size() > eir::kMaxTileLoops) {
+    *why = "more than four tile-loop dims";
+    return false;
+  }
+
+  const int bk = eir::tc_block_k(kind);
+  // BN: minimise waves x (BN + fixed per-tile overhead)
+  int64_t tiles_base = ceil_div(d[mp].size, 128);
+  for (int i : loops) tiles_base *= d[i].size;
+  DeviceState *ds = nullptr;
+  int num_sms = 148;
+  if (device_state(&ds) == EIR_SUCCESS) num_sms = ds->num_sms;
+  int bn = 128;
+  if (kind != 2) {
+    int64_t t128 = tiles_base * ceil_div(d[np].size, 128), t256 = tiles_base * ceil_div(d[np].size, 256);
+    double c128 = (double)ceil_div(t128, num_sms) * (128 + 32);
+    double c256 = (double)ceil_div(t256, num_sms) * (256 + 32);
+    bn = (d[np].size > 128 && c256 <= c128) ? 256 : 128;
+  }
+
+  // TMA maps
+  auto fill_map = [&](eir::MapSpec &ms, bool left, bool mn, int rowdim, int rows) -> bool {
+    ms.dtype = (kind == 0) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    auto st = [&](int i) { return left ? sl_of(i) : sr_of(i); };
+    int first = mn ? rowdim : kp, second = mn ? kp : rowdim;
+    if (st(first) != 1) return false;
+    ms.dims[0] = (uint64_t)d[first].size;
+    ms.dims[1] = (uint64_t)d[second].size;
+    ms.box[0] = mn ? (uint32_t)(128 / esize) : (uint32_t)bk;
+    ms.box[1] = mn ? (uint32_t)bk : (uint32_t)rows;
+    int64_t s1 = st(second) * esize;
+    if (s1 <= 0 || s1 % 16 != 0 || s1 >= (int64_t(1) << 40)) return false;
+    ms.strides_bytes[0] = (uint64_t)s1;
+    int8_t *src = left ? p->tcp.a_src : p->tcp.b_src;
+    for (int j = 0; j < 5; ++j) src[j] = eir::kSrcNone;
+    int slot = 2;
+    int64_t maxs = s1;
+    for (int j = 0; j < (int)ko.size(); ++j) {
+      if (slot > 4) return false;
+      int64_t s = st(ko[j]) * esize;
+      if (s <= 0 || s % 16 != 0 || s >= (int64_t(1) << 40)) return false;
+      ms.dims[slot] = (uint64_t)d[ko[j]].size;
+      ms.strides_bytes[slot - 1] = (uint64_t)s;
+      src[slot] = (int8_t)(eir::kSrcKo0 + j);
+      maxs = std::max(maxs, s);
+      ++slot;
+    }
+    for (int j = 0; j < (int)loops.size(); ++j) {
+      int i = loops[j];
+      bool has = d[i].type == EIR_DIM_C || d[i].type == (left ? EIR_DIM_M : EIR_DIM_N);
+      if (!has) continue;
+      if (slot > 4) return false;
+      int64_t s = st(i) * esize;
+      if (s <= 0 || s % 16 != 0 || s >= (int64_t(1) << 40)) return false;
+      ms.dims[slot] = (uint64_t)d[i].size;
+      ms.strides_bytes[slot - 1] = (uint64_t)s;
+      src[slot] = (int8_t)(eir::kSrcLoop0 + j);
+      maxs = std::max(maxs, s);
+      ++slot;
+    }
+    for (; slot < 5; ++slot) {
+      ms.dims[slot] = 1;
+      ms.strides_bytes[slot - 1] = (uint64_t)maxs;
+    }
+    return true;
+  };
+  if (!fill_map(p->map_a, true, a_mn, mp, 128)) {
+    *why = "left operand strides not TMA-compatible";
+    return false;
+  }
+  if (!fill_map(p->map_b, false, b_mn, np, bn)) {
+    *why = "right operand strides not TMA-compatible";
+    return false;
+  }
+
+  eir::TcParams &t = p->tcp;
+  t.m_size = d[mp].size;
+  t.n_size = d[np].size;
+  t.kp_size = d[kp].size;
+  t.so_m = d[mp].so;
+  t.so_n = d[np].so;
+  t.sa_m = d[mp].sa;
+  t.sa_n = d[np].sa;
+  t.n_loops = (int)loops.size();
+  for (int j = 0; j < eir::kMaxTileLoops; ++j) {
+    t.loop_size[j] = j < t.n_loops ? d[loops[j]].size : 1;
+    t.loop_so[j] = j < t.n_loops ? d[loops[j]].so : 0;
+    t.loop_sa[j] = j < t.n_loops ? d[loops[j]].sa : 0;
+  }
+  t.ko_size[0] = ko.size() > 0 ? d[ko[0]].size : 1;
+  t.ko_size[1] = ko.size() > 1 ? d[ko[1]].size : 1;
+  t.m_tiles = (int32_t)ceil_div(t.m_size, 128);
+  t.n_tiles = (int32_t)ceil_div(t.n_size, bn);
+  t.kp_blocks = (int32_t)ceil_div(t.kp_size, bk);
+  int64_t ksteps = (int64_t)t.kp_blocks * t.ko_size[0] * t.ko_size[1];
+  if (ksteps >= (int64_t(1) << 31)) {
+    *why = "K too large";
+    return false;
+  }
+  t.k_steps = (int32_t)ksteps;
+  t.total_tiles = (int64_t)t.m_tiles * t.n_tiles;
+  for (int j = 0; j < t.n_loops; ++j) t.total_tiles *= t.loop_size[j];
+  t.first_touch = p->first;
+  t.last_touch = p->last;
+
+  p->tc = true;
+  p->tc_kind = kind;
+  p->tc_bn = bn;
+  p->a_mn = a_mn;
+  p->b_mn = b_mn;
+  p->tc_esize = esize;
+  p->prepack = prepack;
+
+  if (prepack >= 0) {
+    bool left = prepack == 0;
+    std::vector<int64_t> sz, si, so;
+    for (int i = 0; i < (int)d.size(); ++i)
+      if (d[i].type == EIR_DIM_C || d[i].type == EIR_DIM_K ||
+          d[i].type == (left ? EIR_DIM_M : EIR_DIM_N)) {
+        sz.push_back(d[i].size);
+        si.push_back(left ? d[i].sl : d[i].sr);
+        so.push_back(packed_stride[i]);
+      }
+    eir_plan *pre = nullptr;
+    int rc = eir_permute_plan_create((int32_t)sz.size(), sz.data(), si.data(), so.data(),
+                                     left ? p->dt_l : p->dt_r, &pre);
+    if (rc != EIR_SUCCESS) {
+      *why = "pre-permute planning failed";
+      p->tc = false;
+      return false;
+    }
+    p->pre = pre;
+    p->ws_bytes = bytes_of(left);
+  }
+
+  char buf[512];
+  std::snprintf(buf, sizeof(buf),
+                "tc kind=%s BN=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d tiles=%lld "
+                "ksteps=%d prepack=%s",
+                kind == 0 ? "bf16" : (kind == 1 ? "tf32" : "3xtf32"), bn, a_mn ? "MN" : "K",
+                b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
+                (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
+                (long long)t.total_tiles, t.k_steps,
+                prepack < 0 ? "none" : (prepack == 0 ? "left" : "right"));
+  *why = buf;
+  return true;
+}
+
+bool valid_first(int k) {
+  return k == EIR_KTYPE_ZERO || k == EIR_KTYPE_COPY || k == EIR_KTYPE_ADD || k == EIR_KTYPE_UNDEFINED;
+}
+bool valid_last(int k) {
+  return k == EIR_KTYPE_RELU || k == EIR_KTYPE_ADD || k == EIR_KTYPE_UNDEFINED;
+}
+
+int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+             cudaStream_t st) {
+  cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt, l, r, aux, out, st);
+  if (e != cudaSuccess) return cuda_fail(e, "simt contraction launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
+
+}  // namespace
+
+// =================================================================== C-ABI
+extern "C" {
+
+int eir_version(void) { return 1; }
+
+char const *eir_last_error_string(void) { return g_last_error.c_str(); }
+
+int64_t eir_launch_count(void) { return g_launches.load(); }
+
+int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out) {
+  if (desc == nullptr || plan_out == nullptr)
+    return set_error(EIR_INVALID_ARGUMENT, "null descriptor or plan pointer");
+  *plan_out = nullptr;
+  if (desc->num_dims < 0 || (desc->num_dims > 0 && desc->dims == nullptr))
+    return set_error(EIR_INVALID_ARGUMENT, "bad dims");
+  const int dl = desc->dtype_left, dr = desc->dtype_right, dout = desc->dtype_out;
+  bool dt_ok = (dout == EIR_FP64 && dl == EIR_FP64 && dr == EIR_FP64) ||
+               (dout == EIR_FP32 && (dl == EIR_FP32 || dl == EIR_BF16) &&
+                (dr == EIR_FP32 || dr == EIR_BF16));
+  if (!dt_ok) return set_error(EIR_INVALID_DTYPE, "unsupported dtype combination");
+  if (desc->dtype_comp < EIR_COMPUTE_DEFAULT || desc->dtype_comp > EIR_COMPUTE_BF16)
+    return set_error(EIR_INVALID_DTYPE, "unsupported compute type");
+  if (dout == EIR_FP64 && desc->dtype_comp != EIR_COMPUTE_DEFAULT && desc->dtype_comp != EIR_COMPUTE_FP64)
+    return set_error(EIR_INVALID_DTYPE, "FP64 data needs FP64 compute");
+  if (!valid_first(desc->ktype_first_touch) || desc->ktype_main != EIR_KTYPE_MADD ||
+      !valid_last(desc->ktype_last_touch))
+    return set_error(EIR_INVALID_KTYPE, "unsupported kernel type");
+  bool uses_aux = desc->ktype_first_touch == EIR_KTYPE_COPY || desc->ktype_first_touch == EIR_KTYPE_ADD ||
+                  desc->ktype_last_touch == EIR_KTYPE_ADD;
+
+  eir_plan *p = new eir_plan();
+  p->what = 1;
+  p->dt_l = dl;
+  p->dt_r = dr;
+  p->dt_o = dout;
+  p->comp = desc->dtype_comp;
+  p->first = desc->ktype_first_touch;
+  p->last = desc->ktype_last_touch;
+  p->desc_flags = desc->flags;
+
+  std::vector<LDim> dims;
+  int64_t sc = 1, sm = 1, sn = 1, sk = 1;
+  for (int i = 0; i < desc->num_dims; ++i) {
+    eir_dim const &x = desc->dims[i];
+    if (x.type < EIR_DIM_C || x.type > EIR_DIM_K || x.size < 0) {
+      delete p;
+      return set_error(EIR_INVALID_ARGUMENT, "bad dim type or size");
+    }
+    LDim y;
+    y.type = x.type;
+    y.size = x.size;
+    y.sl = (x.type == EIR_DIM_N) ? 0 : x.stride_left;
+    y.sr = (x.type == EIR_DIM_M) ? 0 : x.stride_right;
+    y.so = (x.type == EIR_DIM_K) ? 0 : x.stride_out;
+    y.sa = (x.type == EIR_DIM_K || !uses_aux) ? 0 : x.stride_out_aux;
+    if (x.size == 0 && x.type != EIR_DIM_K) p->empty = true;
+    (x.type == EIR_DIM_C ? sc : x.type == EIR_DIM_M ? sm : x.type == EIR_DIM_N ? sn : sk) *= x.size;
+    dims.push_back(y);
+  }
+  p->num_ops = 2 * sc * sm * sn * sk;
+  if (p->first == EIR_KTYPE_ZERO) p->num_ops -= sc * sm * sn;
+
+  p->dims = simplify_dims(dims);
+  for (int ty = EIR_DIM_C; ty <= EIR_DIM_K; ++ty) {
+    eir::GroupDims *g = ty == EIR_DIM_C ? &p->simt.c : ty == EIR_DIM_M ? &p->simt.m
+                      : ty == EIR_DIM_N ? &p->simt.n : &p->simt.k;
+    if (build_group(p->dims, ty, g) != 0) {
+      delete p;
+      return set_error(EIR_COMPILATION_FAILED, "too many non-fusable dims of one type");
+    }
+  }
+  p->simt.first_touch = p->first;
+  p->simt.last_touch = p->last;
+  p->simt.a_kfast = min_abs_stride(p->dims, EIR_DIM_K, true) < min_abs_stride(p->dims, EIR_DIM_M, true);
+  p->simt.b_kfast = min_abs_stride(p->dims, EIR_DIM_K, false) < min_abs_stride(p->dims, EIR_DIM_N, false);
+  p->simt.m_tiles = ceil_div(p->simt.m.total, 64);
+  p->simt.n_tiles = ceil_div(p->simt.n.total, 64);
+
+  std::string why = "forced";
+  if (!p->empty && !(desc->flags & EIR_FLAG_FORCE_SIMT) && try_tc(p, &why)) {
+    p->family = EIR_FAMILY_TC;
+  } else {
+    p->family = EIR_FAMILY_SIMT;
+  }
+  std::string dims_txt;
+  for (auto const &x : p->dims) {
+    dims_txt += type_name(x.type);
+    dims_txt += std::to_string(x.size) + " ";
+  }
+  p->text = (p->family == EIR_FAMILY_TC ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
+  *plan_out = p;
+  return EIR_SUCCESS;
+}
+
+int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, void *out, void *stream) {
+  if (p == nullptr || p->what != 1) return set_error(EIR_INVALID_ARGUMENT, "not a contraction plan");
+  if (p->empty) return EIR_SUCCESS;
+  if (l == nullptr || r == nullptr || out == nullptr)
+    return set_error(EIR_NO_DATA_PTR_PROVIDED, "null operand pointer");
+  bool uses_aux = p->first == EIR_KTYPE_COPY || p->first == EIR_KTYPE_ADD || p->last == EIR_KTYPE_ADD;
+  if (uses_aux && aux == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->family != EIR_FAMILY_TC) return run_simt(p, l, r, aux, out, st);
+
+  DeviceState *ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != EIR_SUCCESS) return rc;
+  // TMA needs 16-byte aligned bases; otherwise take the generic path
+  if ((reinterpret_cast<uintptr_t>(l) & 15) || (reinterpret_cast<uintptr_t>(r) & 15))
+    return run_simt(p, l, r, aux, out, st);
+
+  void const *a_ptr = l, *b_ptr = r;
+  if (p->prepack >= 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (p->ws == nullptr || p->ws_device != dev) {
+      if (p->ws != nullptr) cudaFree(p->ws);
+      cudaError_t e = cudaMalloc(&p->ws, (size_t)p->ws_bytes);
+      if (e != cudaSuccess) {
+        p->ws = nullptr;
+        return cuda_fail(e, "cudaMalloc(workspace)");
+      }
+      p->ws_device = dev;
+    }
+    void const *src = p->prepack == 0 ? l : r;
+    rc = eir_permute(p->pre, src, p->ws, stream);
+    if (rc != EIR_SUCCESS) return rc;
+    (p->prepack == 0 ? a_ptr : b_ptr) = p->ws;
+  }
+
+  CUtensorMap ma, mb;
+  {
+    std::lock_guard<std::mutex> lk(p->mu);
+    if (p->cache_a.ptr != a_ptr) {
+      rc = encode_map(p->map_a, a_ptr, &p->cache_a.map);
+      if (rc != EIR_SUCCESS) {
+        p->cache_a.ptr = nullptr;
+        return rc;
+      }
+      p->cache_a.ptr = a_ptr;
+    }
+    if (p->cache_b.ptr != b_ptr) {
+      rc = encode_map(p->map_b, b_ptr, &p->cache_b.map);
+      if (rc != EIR_SUCCESS) {
+        p->cache_b.ptr = nullptr;
+        return rc;
+      }
+      p->cache_b.ptr = b_ptr;
+    }
+    ma = p->cache_a.map;
+    mb = p->cache_b.map;
+  }
+  eir::TcParams tp = p->tcp;
+  tp.err = ds->err;
+  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->a_mn, p->b_mn, ma, mb, tp,
+                                          static_cast<float const *>(aux), static_cast<float *>(out),
+                                          ds->num_sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
+
+int64_t eir_contract_num_ops(eir_plan const *p) { return (p && p->what == 1) ? p->num_ops : 0; }
+
+int eir_permute_plan_create(int32_t nd, int64_t const *sizes, int64_t const *sin,
+                            int64_t const *sout, int32_t dtype, eir_plan **plan_out) {
+  if (plan_out == nullptr) return set_error(EIR_INVALID_ARGUMENT, "null plan pointer");
+  *plan_out = nullptr;
+  if (nd < 0 || (nd > 0 && (sizes == nullptr || sin == nullptr || sout == nullptr)))
+    return set_error(EIR_INVALID_ARGUMENT, "bad permute dims");
+  int64_t es = dtype_bytes(dtype);
+  if (es < 0) return set_error(EIR_INVALID_DTYPE, "unsupported permute dtype");
+  eir_plan *p = new eir_plan();
+  p->what = 2;
+  p->family = EIR_FAMILY_PERMUTE;
+  p->esize = (int)es;
+  int rc = plan_permute(nd, sizes, sin, sout, (int)es, &p->perm, &p->text);
+  if (rc != EIR_SUCCESS) {
+    delete p;
+    return rc;
+  }
+  *plan_out = p;
+  return EIR_SUCCESS;
+}
+
+int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
+  if (p == nullptr || p->what != 2) return set_error(EIR_INVALID_ARGUMENT, "not a permute plan");
+  if (p->perm.total == 0) return EIR_SUCCESS;
+  if (in == nullptr || out == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null pointer");
+  DeviceState *ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != EIR_SUCCESS) return rc;
+  eir::PermuteParams pp = p->perm;
+  if (pp.mode == 0 && pp.vec > 1 &&
+      ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % (pp.vec * p->esize)))
+    pp.vec = 1;
+  cudaError_t e = eir::launch_permute(p->esize, pp, in, out, ds->num_sms,
+                                      static_cast<cudaStream_t>(stream));
+  if (e != cudaSuccess) return cuda_fail(e, "permute launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
+
+int eir_plan_destroy(eir_plan *p) {
+  if (p == nullptr) return EIR_SUCCESS;
+  if (p->pre) eir_plan_destroy(p->pre);
+  if (p->ws) {
+    int cur = 0;
+    cudaGetDevice(&cur);
+    if (p->ws_device >= 0 && p->ws_device != cur) cudaSetDevice(p->ws_device);
+    cudaFree(p->ws);
+    if (p->ws_device >= 0 && p->ws_device != cur) cudaSetDevice(cur);
+  }
+  delete p;
+  return EIR_SUCCESS;
+}
+
+int eir_plan_kernel_family(eir_plan const *p) { return p ? p->family : EIR_FAMILY_NONE; }
+
+int64_t eir_plan_workspace_bytes(eir_plan const *p) { return p ? p->ws_bytes : 0; }
+
+char const *eir_plan_describe(eir_plan const *p) { return p ? p->text.c_str() : ""; }
+
+int eir_check_device_errors(void *stream) {
+  DeviceState *ds = nullptr;
+  int rc = device_state(&ds);
+  if (rc != EIR_SUCCESS) return rc;
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  cudaError_t e = cudaStreamSynchronize(st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
+  uint32_t h = 0;
+  e = cudaMemcpy(&h, ds->err, sizeof(h), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(error word)");
+  if (h != 0) {
+    cudaMemset(ds->err, 0, sizeof(uint32_t));
+    char buf[96];
+    std::snprintf(buf, sizeof(buf), "device wait timed out (code 0x%x)", h);
+    return set_error(EIR_DEVICE_TIMEOUT, buf);
+  }
+  return EIR_SUCCESS;
+}
+
+}  // extern "C"

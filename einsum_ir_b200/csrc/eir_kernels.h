@@ -1,0 +1,23 @@
+// Host-callable launchers of the device kernels (internal to the library).
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include "eir_params.h"
+
+namespace eir {
+
+cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const &p, void const *l,
+                                 void const *r, void const *aux, void *out, cudaStream_t st);
+
+cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,
+                           int num_sms, cudaStream_t st);
+
+// kind: 0 = BF16 (kind::f16), 1 = TF32, 2 = 3xTF32 (FP32-accurate)
+cudaError_t launch_tc_contract(int kind, int bn, bool a_mn, bool b_mn, CUtensorMap const &ma,
+                               CUtensorMap const &mb, TcParams const &p, float const *aux,
+                               float *out, int num_sms, cudaStream_t st);
+
+int tc_block_k(int kind);
+
+}  // namespace eir

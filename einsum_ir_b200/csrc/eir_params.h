@@ -1,0 +1,75 @@
+// Kernel parameter blocks shared by the planner (host) and the kernels.
+// All strides are in elements.
+#pragma once
+
+#include <cstdint>
+
+namespace eir {
+
+constexpr int kMaxGroupDims = 6;   // dims per C/M/N/K group in the SIMT kernel
+constexpr int kMaxPermDims = 8;    // dims of a permute after fusion
+
+// A group of loop dimensions flattened into one index; dim 0 varies fastest.
+struct GroupDims {
+  int32_t n = 0;
+  int32_t pad_ = 0;
+  int64_t total = 1;
+  int64_t size[kMaxGroupDims] = {};
+  int64_t sl[kMaxGroupDims] = {};   // left strides
+  int64_t sr[kMaxGroupDims] = {};   // right strides
+  int64_t so[kMaxGroupDims] = {};   // out strides
+  int64_t sa[kMaxGroupDims] = {};   // out_aux strides
+};
+
+struct SimtParams {
+  GroupDims c, m, n, k;
+  int32_t first_touch;  // EIR_KTYPE_*
+  int32_t last_touch;
+  int32_t a_kfast;      // left: K is the fast (stride-1) direction -> load along K
+  int32_t b_kfast;      // right: K is the fast direction
+  int64_t m_tiles, n_tiles;
+};
+
+// Permute: dims sorted so that dim 0 is the output's fastest dim.
+struct PermuteParams {
+  int32_t nd = 0;
+  int32_t mode = 0;        // 0 = copy along the shared stride-1 dim, 1 = 2-D tile transpose
+  int32_t vec = 1;         // elements per vector access (copy mode)
+  int32_t tdim_in = 0;     // transpose: index of the input's fastest dim
+  int64_t size[kMaxPermDims] = {};
+  int64_t sin[kMaxPermDims] = {};
+  int64_t sout[kMaxPermDims] = {};
+  int64_t total = 1;       // number of elements
+  int64_t rows = 1;        // copy mode: number of rows (elements / size[0])
+  int64_t batch = 1;       // transpose mode: number of (size[0] x size[tdim_in]) slices
+};
+
+// tcgen05 contraction. Operand tensor maps are 5-D; map dims 0/1 are the
+// primitive (K / row) dims, dims 2..4 take their coordinate from `*_src`.
+enum : int8_t {
+  kSrcNone = 0,   // coordinate 0 (padding dim of size 1)
+  kSrcKo0 = 1,
+  kSrcKo1 = 2,
+  kSrcLoop0 = 3,  // .. kSrcLoop0 + 3
+};
+
+constexpr int kMaxTileLoops = 4;
+
+struct TcParams {
+  int64_t m_size, n_size, kp_size;          // primitive M / N / K sizes
+  int64_t so_m, so_n, sa_m, sa_n;           // out / aux strides of the primitive M and N dims
+  int64_t loop_size[kMaxTileLoops];
+  int64_t loop_so[kMaxTileLoops];
+  int64_t loop_sa[kMaxTileLoops];
+  int64_t ko_size[2];
+  int64_t total_tiles;
+  int32_t m_tiles, n_tiles, kp_blocks, k_steps;
+  int32_t n_loops;
+  int32_t first_touch, last_touch;
+  int8_t a_src[5];
+  int8_t b_src[5];
+  int16_t pad_;
+  uint32_t *err;                            // device error word
+};
+
+}  // namespace eir

@@ -1,0 +1,69 @@
+// Internal plan objects behind the opaque `eir_plan` handle of the C-ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <cstdint>
+#include <mutex>
+#include <string>
+#include <vector>
+#include "eir_params.h"
+#include "../../include/eir_cuda.h"
+
+namespace eir {
+
+// one loop dim after lowering (element strides)
+struct LDim {
+  int type = 0;
+  int64_t size = 1;
+  int64_t sl = 0, sr = 0, so = 0, sa = 0;
+};
+
+// a rank-5 TMA map with the data pointer bound at run time
+struct MapSpec {
+  int rank = 5;
+  uint64_t dims[5] = {1, 1, 1, 1, 1};
+  uint64_t strides_bytes[4] = {16, 16, 16, 16};  // strides of dims 1..4
+  uint32_t box[5] = {1, 1, 1, 1, 1};
+  CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+};
+
+struct TensorMapCache {
+  void const *ptr = nullptr;
+  CUtensorMap map;
+};
+
+}  // namespace eir
+
+struct eir_plan {
+  int what = 0;  // 1 = contraction, 2 = permute
+  int family = EIR_FAMILY_NONE;
+  int64_t num_ops = 0;
+  std::string text;
+
+  // ---- contraction
+  int dt_l = 0, dt_r = 0, dt_o = 0, comp = 0, first = 99, last = 99;
+  int desc_flags = 0;
+  bool empty = false;            // nothing to compute (a C/M/N dim of size 0)
+  std::vector<eir::LDim> dims;   // after size-1 removal and fusion
+  eir::SimtParams simt;
+  bool tc = false;
+  int tc_kind = 0, tc_bn = 128;
+  bool a_mn = false, b_mn = false;
+  eir::TcParams tcp{};
+  eir::MapSpec map_a, map_b;
+  int tc_esize = 2;
+  std::mutex mu;                 // guards the tensor-map caches
+  eir::TensorMapCache cache_a, cache_b;
+
+  // operand pre-permute into the plan's workspace (0 = left, 1 = right, -1 = none)
+  int prepack = -1;
+  eir_plan *pre = nullptr;
+  void *ws = nullptr;
+  int64_t ws_bytes = 0;
+  int ws_device = -1;
+
+  // ---- permute
+  eir::PermuteParams perm;
+  int esize = 4;
+};

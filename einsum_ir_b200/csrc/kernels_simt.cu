@@ -1,0 +1,318 @@
+// CUDA-core kernels: the generic strided contraction (any layout, FP32/FP64
+// accumulate, BF16/FP32/FP64 inputs) and the permute (Unary COPY) kernels.
+//
+// The generic contraction flattens each dim group (C, M, N, K) into one index
+// and decomposes it with per-dim sizes/strides, so it reads every operand in
+// place whatever its strides are; it is the path for contractions the tensor
+// core lowering does not take (tiny trees, K = empty outer products, FP64
+// until the DMMA kernel, unaligned strides). Semantics follow the reference's
+// scalar loop engine: out = first_touch(out, aux); out += sum_K l*r;
+// out = last_touch(out, aux) (ContractionBackendScalar.cpp:4-143,
+// ContractionBackend.cpp:296-348,495-515, ContractionBackendTpp.cpp:130-163).
+#include "eir_common.cuh"
+#include "eir_params.h"
+#include "eir_kernels.h"
+
+namespace eir {
+
+template <typename T>
+__device__ __forceinline__ float to_f32(T x) {
+  return static_cast<float>(x);
+}
+template <>
+__device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 x) {
+  return __bfloat162float(x);
+}
+
+template <typename TA, typename T>
+__device__ __forceinline__ TA to_acc(T x) {
+  return static_cast<TA>(to_f32(x));
+}
+template <>
+__device__ __forceinline__ double to_acc<double, double>(double x) {
+  return x;
+}
+
+__device__ __forceinline__ void decompose(GroupDims const &g, int64_t x, int64_t &ol, int64_t &orr,
+                                          int64_t &oo, int64_t &oa) {
+  ol = orr = oo = oa = 0;
+#pragma unroll
+  for (int d = 0; d < kMaxGroupDims; ++d) {
+    if (d < g.n) {
+      int64_t i = x % g.size[d];
+      x /= g.size[d];
+      ol += i * g.sl[d];
+      orr += i * g.sr[d];
+      oo += i * g.so[d];
+      oa += i * g.sa[d];
+    }
+  }
+}
+
+constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16;
+
+template <typename TL, typename TR, typename TO, typename TA>
+__global__ void __launch_bounds__(256)
+    simt_contract_kernel(const SimtParams p, const TL *__restrict__ L, const TR *__restrict__ R,
+                         const TO *__restrict__ AUX, TO *__restrict__ OUT) {
+  constexpr int BM = kSimtBM, BN = kSimtBN, BK = kSimtBK;
+  __shared__ TA As[BK][BM + 1];
+  __shared__ TA Bs[BK][BN + 1];
+  __shared__ int64_t row_l[BM], row_o[BM], row_a[BM];
+  __shared__ int64_t col_r[BN], col_o[BN], col_a[BN];
+  __shared__ int64_t k_l[BK], k_r[BK];
+
+  const int tid = threadIdx.x;
+  const int tx = tid & 15, ty = tid >> 4;
+  int64_t bid = blockIdx.x;
+  const int64_t mt = bid % p.m_tiles;
+  bid /= p.m_tiles;
+  const int64_t nt = bid % p.n_tiles;
+  const int64_t ct = bid / p.n_tiles;
+
+  const int64_t M = p.m.total, N = p.n.total, K = p.k.total;
+  int64_t c_l, c_r, c_o, c_a;
+  decompose(p.c, ct, c_l, c_r, c_o, c_a);
+
+  if (tid < BM) {
+    int64_t m = mt * BM + tid;
+    int64_t ol = 0, orr, oo = 0, oa = 0;
+    if (m < M) decompose(p.m, m, ol, orr, oo, oa);
+    row_l[tid] = ol + c_l;
+    row_o[tid] = oo + c_o;
+    row_a[tid] = oa + c_a;
+  } else if (tid < BM + BN) {
+    int t = tid - BM;
+    int64_t n = nt * BN + t;
+    int64_t ol, orr = 0, oo = 0, oa = 0;
+    if (n < N) decompose(p.n, n, ol, orr, oo, oa);
+    col_r[t] = orr + c_r;
+    col_o[t] = oo;
+    col_a[t] = oa;
+  }
+
+  TA acc[4][4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[i][j] = TA(0);
+
+  for (int64_t k0 = 0; k0 < K; k0 += BK) {
+    if (tid < BK) {
+      int64_t k = k0 + tid;
+      int64_t ol = 0, orr = 0, oo, oa;
+      if (k < K) decompose(p.k, k, ol, orr, oo, oa);
+      k_l[tid] = ol;
+      k_r[tid] = orr;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int q = 0; q < (BM * BK) / 256; ++q) {
+      int e = tid + 256 * q;
+      int kk, mm;
+      if (p.a_kfast) {
+        kk = e % BK;
+        mm = e / BK;
+      } else {
+        mm = e % BM;
+        kk = e / BM;
+      }
+      int64_t m = mt * BM + mm, k = k0 + kk;
+      As[kk][mm] = (m < M && k < K) ? to_acc<TA>(L[row_l[mm] + k_l[kk]]) : TA(0);
+    }
+#pragma unroll
+    for (int q = 0; q < (BN * BK) / 256; ++q) {
+      int e = tid + 256 * q;
+      int kk, nn;
+      if (p.b_kfast) {
+        kk = e % BK;
+        nn = e / BK;
+      } else {
+        nn = e % BN;
+        kk = e / BN;
+      }
+      int64_t n = nt * BN + nn, k = k0 + kk;
+      Bs[kk][nn] = (n < N && k < K) ? to_acc<TA>(R[col_r[nn] + k_r[kk]]) : TA(0);
+    }
+    __syncthreads();
+#pragma unroll
+    for (int kk = 0; kk < BK; ++kk) {
+      TA a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[kk][tx + 16 * i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Bs[kk][ty + 16 * j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
+    }
+    __syncthreads();
+  }
+
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int mm = tx + 16 * i;
+    const int64_t m = mt * BM + mm;
+    if (m >= M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int nn = ty + 16 * j;
+      const int64_t n = nt * BN + nn;
+      if (n >= N) continue;
+      const int64_t o = row_o[mm] + col_o[nn];
+      const int64_t a = row_a[mm] + col_a[nn];
+      TA x = acc[i][j];
+      if (p.first_touch == 3 /*COPY*/) x += static_cast<TA>(AUX[a]);
+      else if (p.first_touch == 2 /*ADD*/) x += static_cast<TA>(OUT[o]) + static_cast<TA>(AUX[a]);
+      else if (p.first_touch != 0 /*ZERO*/) x += static_cast<TA>(OUT[o]);
+      if (p.last_touch == 1 /*RELU*/) x = x > TA(0) ? x : TA(0);
+      else if (p.last_touch == 2 /*ADD*/) x += static_cast<TA>(AUX[a]);
+      OUT[o] = static_cast<TO>(x);
+    }
+  }
+}
+
+template <typename TL, typename TR, typename TO, typename TA>
+static cudaError_t launch_simt_t(SimtParams const &p, void const *l, void const *r,
+                                 void const *aux, void *out, cudaStream_t st) {
+  int64_t blocks = p.m_tiles * p.n_tiles * p.c.total;
+  if (blocks <= 0) return cudaSuccess;
+  if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
+  simt_contract_kernel<TL, TR, TO, TA><<<(unsigned)blocks, 256, 0, st>>>(
+      p, static_cast<TL const *>(l), static_cast<TR const *>(r), static_cast<TO const *>(aux),
+      static_cast<TO *>(out));
+  return cudaGetLastError();
+}
+
+// dtypes: 0 = FP32, 1 = FP64, 2 = BF16 (values of the C-ABI enum)
+cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const &p, void const *l,
+                                 void const *r, void const *aux, void *out, cudaStream_t st) {
+  if (dt_o == 1) {
+    if (dt_l == 1 && dt_r == 1) return launch_simt_t<double, double, double, double>(p, l, r, aux, out, st);
+    return cudaErrorInvalidValue;
+  }
+  if (dt_o != 0) return cudaErrorInvalidValue;
+  if (dt_l == 0 && dt_r == 0) return launch_simt_t<float, float, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 2 && dt_r == 2)
+    return launch_simt_t<__nv_bfloat16, __nv_bfloat16, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 2 && dt_r == 0)
+    return launch_simt_t<__nv_bfloat16, float, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 0 && dt_r == 2)
+    return launch_simt_t<float, __nv_bfloat16, float, float>(p, l, r, aux, out, st);
+  return cudaErrorInvalidValue;
+}
+
+// ------------------------------------------------------------------ permute
+// copy mode: dim 0 is stride-1 in input and output; V elements per access
+template <typename T, int V>
+__global__ void __launch_bounds__(256)
+    permute_copy_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
+  struct alignas(sizeof(T) * V) Vec {
+    T v[V];
+  };
+  const int64_t n0v = p.size[0] / V;
+  const int64_t total = p.rows * n0v;
+  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
+       g += (int64_t)gridDim.x * blockDim.x) {
+    int64_t i0 = g % n0v;
+    int64_t row = g / n0v;
+    int64_t oi = 0, oo = 0;
+#pragma unroll
+    for (int d = 1; d < kMaxPermDims; ++d) {
+      if (d < p.nd) {
+        int64_t i = row % p.size[d];
+        row /= p.size[d];
+        oi += i * p.sin[d];
+        oo += i * p.sout[d];
+      }
+    }
+    // V > 1 only when dim 0 has unit stride on both sides (checked by the planner)
+    *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) =
+        *reinterpret_cast<Vec const *>(in + oi + i0 * V * p.sin[0]);
+  }
+}
+
+// transpose mode: dim 0 is the output's stride-1 dim, dim tdim_in the input's
+template <typename T>
+__global__ void __launch_bounds__(256)
+    permute_transpose_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
+  constexpr int TS = 32;
+  __shared__ T tile[TS][TS + 1];
+  const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
+  const int td = p.tdim_in;
+  const int64_t s0 = p.size[0], st = p.size[td];
+  const int64_t t0 = (s0 + TS - 1) / TS, tt = (st + TS - 1) / TS;
+  const int64_t nblk = t0 * tt * p.batch;
+  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
+    int64_t b0 = blk % t0;
+    int64_t r = blk / t0;
+    int64_t bt = r % tt;
+    int64_t bat = r / tt;
+    int64_t oi = 0, oo = 0;
+#pragma unroll
+    for (int d = 1; d < kMaxPermDims; ++d) {
+      if (d < p.nd && d != td) {
+        int64_t i = bat % p.size[d];
+        bat /= p.size[d];
+        oi += i * p.sin[d];
+        oo += i * p.sout[d];
+      }
+    }
+    // load: consecutive threads walk the input's stride-1 dim
+#pragma unroll
+    for (int i = 0; i < TS / 8; ++i) {
+      int64_t it = bt * TS + tx, i0 = b0 * TS + ty + 8 * i;
+      if (it < st && i0 < s0) tile[ty + 8 * i][tx] = in[oi + it * p.sin[td] + i0 * p.sin[0]];
+    }
+    __syncthreads();
+    // store: consecutive threads walk the output's stride-1 dim
+#pragma unroll
+    for (int i = 0; i < TS / 8; ++i) {
+      int64_t i0 = b0 * TS + tx, it = bt * TS + ty + 8 * i;
+      if (it < st && i0 < s0) out[oo + i0 * p.sout[0] + it * p.sout[td]] = tile[tx][ty + 8 * i];
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T>
+static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void *out, int num_sms,
+                                    cudaStream_t st) {
+  if (p.total == 0) return cudaSuccess;
+  const T *i = static_cast<T const *>(in);
+  T *o = static_cast<T *>(out);
+  if (p.mode == 0) {
+    int64_t work = p.total / p.vec;
+    int64_t blocks = (work + 255) / 256;
+    int64_t cap = (int64_t)num_sms * 16;
+    if (blocks > cap) blocks = cap;
+    if (blocks < 1) blocks = 1;
+    switch (p.vec) {
+      case 1: permute_copy_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
+      case 2: permute_copy_kernel<T, 2><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
+      case 4: permute_copy_kernel<T, 4><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
+      case 8: permute_copy_kernel<T, 8><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
+      default: return cudaErrorInvalidValue;
+    }
+  } else {
+    int64_t nblk = ((p.size[0] + 31) / 32) * ((p.size[p.tdim_in] + 31) / 32) * p.batch;
+    int64_t cap = (int64_t)num_sms * 8;
+    int64_t blocks = nblk < cap ? nblk : cap;
+    if (blocks < 1) blocks = 1;
+    permute_transpose_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(p, i, o);
+  }
+  return cudaGetLastError();
+}
+
+cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,
+                           int num_sms, cudaStream_t st) {
+  switch (esize) {
+    case 2: return launch_permute_t<uint16_t>(p, in, out, num_sms, st);
+    case 4: return launch_permute_t<uint32_t>(p, in, out, num_sms, st);
+    case 8: return launch_permute_t<uint64_t>(p, in, out, num_sms, st);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
+}  // namespace eir

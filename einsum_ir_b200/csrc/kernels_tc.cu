@@ -1,0 +1,426 @@
+// tcgen05 (5th-gen tensor core) strided binary contraction for sm_100a.
+//
+// One persistent CTA per SM walks output tiles of 128 (primitive M) x BN
+// (primitive N). The remaining C / M / N dims are "tile loops" (scheduler
+// coordinates); the K range is the primitive K dim (blocked by BK) times up
+// to two outer K dims. Operands are read in their native strided layouts by
+// 5-D TMA tensor maps (128B swizzle, K-major or MN-major per operand), staged
+// in a shared-memory ring and consumed by tcgen05.mma issued from one thread,
+// with the FP32 accumulator in TMEM (double buffered, so the epilogue of one
+// tile overlaps the main loop of the next).
+//
+// Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+TMEM owner),
+// warps 2..5 = epilogue (TMEM -> registers -> global, fused first/last touch:
+// ZERO/COPY/ADD before, RELU/ADD after, aux read through broadcast strides),
+// warps 6..9 (3xTF32 only) = split each staged FP32 tile into hi + lo TF32
+// parts in shared memory (hi = round-to-nearest TF32, lo = x - hi) so three
+// MMAs (hi*hi + hi*lo + lo*hi) give an FP32-accurate product.
+//
+// Semantics follow the reference loop engine: first touch at the first K
+// step, last touch after the last (ContractionBackend.cpp:296-348,495-515;
+// ContractionBackendTpp.cpp:15-62,80-163).
+#include <cuda.h>
+#include "eir_common.cuh"
+#include "eir_params.h"
+#include "eir_kernels.h"
+
+namespace eir {
+
+enum { kKindBF16 = 0, kKindTF32 = 1, kKind3xTF32 = 2 };
+
+template <int KIND, int BN>
+struct TcConfig {
+  static constexpr int kEsize = (KIND == kKindBF16) ? 2 : 4;
+  static constexpr int kBM = 128;
+  static constexpr int kBK = 128 / kEsize;                 // one 128-byte swizzle row of K
+  static constexpr int kMmaK = (KIND == kKindBF16) ? 16 : 8;
+  static constexpr int kRowsPerBox = 128 / kEsize;         // MN-major: rows per 128B box
+  static constexpr int kABytes = kBM * 128;
+  static constexpr int kBBytes = BN * 128;
+  static constexpr bool kSplit = (KIND == kKind3xTF32);
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
+  static constexpr int kStages = (KIND == kKind3xTF32) ? 3 : (196608 / kStageBytes);
+  static constexpr int kThreads = kSplit ? 320 : 192;
+  static constexpr int kTmemCols = 2 * BN;                 // double-buffered accumulator
+  static constexpr int kBarBytes = 256;
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+};
+
+// instruction descriptor for kind::f16 (bf16) / kind::tf32, FP32 accumulate
+__host__ __device__ constexpr uint32_t make_idesc(int kind, int m, int n, bool a_mn, bool b_mn) {
+  uint32_t fmt = (kind == kKindBF16) ? 1u : 2u;  // BF16 = 1, TF32 = 2
+  return (1u << 4)                               // D format F32
+         | (fmt << 7) | (fmt << 10)              // A / B format
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
+         | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+struct TileCoord {
+  int64_t mt, nt;
+  int64_t l[kMaxTileLoops];
+};
+
+__device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
+  TileCoord c;
+  c.mt = t % p.m_tiles;
+  t /= p.m_tiles;
+  c.nt = t % p.n_tiles;
+  t /= p.n_tiles;
+#pragma unroll
+  for (int i = 0; i < kMaxTileLoops; ++i) {
+    if (i < p.n_loops) {
+      c.l[i] = t % p.loop_size[i];
+      t /= p.loop_size[i];
+    } else {
+      c.l[i] = 0;
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, TileCoord const &c) {
+  switch (src) {
+    case kSrcKo0: return (int)ko0;
+    case kSrcKo1: return (int)ko1;
+    case kSrcLoop0: return (int)c.l[0];
+    case kSrcLoop0 + 1: return (int)c.l[1];
+    case kSrcLoop0 + 2: return (int)c.l[2];
+    case kSrcLoop0 + 3: return (int)c.l[3];
+    default: return 0;
+  }
+}
+
+__device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
+  uint32_t r;
+  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
+  return r;
+}
+
+template <int KIND, int BN, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
+    tc_contract_kernel(const __grid_constant__ CUtensorMap map_a,
+                       const __grid_constant__ CUtensorMap map_b, const TcParams p,
+                       const float *__restrict__ aux, float *__restrict__ out) {
+  using Cfg = TcConfig<KIND, BN>;
+  constexpr int S = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
+  constexpr int BM = Cfg::kBM;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;                                  // S x kABytes
+  uint8_t *sB = sA + S * Cfg::kABytes;                 // S x kBBytes
+  uint8_t *sAlo = sB + S * Cfg::kBBytes;               // (split) S x kABytes
+  uint8_t *sBlo = sAlo + (Cfg::kSplit ? S * Cfg::kABytes : 0);
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
+  uint64_t *full = bars;            // S
+  uint64_t *empty = bars + S;       // S
+  uint64_t *conv = bars + 2 * S;    // S (split only)
+  uint64_t *tfull = bars + 3 * S;   // 2
+  uint64_t *tempty = bars + 3 * S + 2;  // 2
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 4);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+      mbar_init(&conv[s], 128);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  if (warp == 1) tmem_alloc(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
+        TileCoord c = decode_tile(p, t);
+        for (int ks = 0; ks < p.k_steps; ++ks) {
+          int kp = ks % p.kp_blocks;
+          int64_t r = ks / p.kp_blocks;
+          int64_t ko0 = r % p.ko_size[0];
+          int64_t ko1 = r / p.ko_size[0];
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
+            if (!*abort_flag) record_error(p.err, kErrTimeoutProducer);
+            *abort_flag = 1;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], Cfg::kABytes + Cfg::kBBytes);
+          int a2 = src_coord(p.a_src[2], ko0, ko1, c), a3 = src_coord(p.a_src[3], ko0, ko1, c),
+              a4 = src_coord(p.a_src[4], ko0, ko1, c);
+          int b2 = src_coord(p.b_src[2], ko0, ko1, c), b3 = src_coord(p.b_src[3], ko0, ko1, c),
+              b4 = src_coord(p.b_src[4], ko0, ko1, c);
+          uint8_t *dA = sA + stage * Cfg::kABytes;
+          uint8_t *dB = sB + stage * Cfg::kBBytes;
+          int mrow = (int)(c.mt * BM), nrow = (int)(c.nt * BN), kcol = kp * BK;
+          if (!A_MN) {
+            tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
+              tma_load_5d(dA + j * BK * 128, &map_a, &full[stage], mrow + j * Cfg::kRowsPerBox,
+                          kcol, a2, a3, a4);
+          }
+          if (!B_MN) {
+            tma_load_5d(dB, &map_b, &full[stage], kcol, nrow, b2, b3, b4);
+          } else {
+#pragma unroll
+            for (int j = 0; j < BN / Cfg::kRowsPerBox; ++j)
+              tma_load_5d(dB + j * BK * 128, &map_b, &full[stage], nrow + j * Cfg::kRowsPerBox,
+                          kcol, b2, b3, b4);
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = make_idesc(KIND, BM, BN, A_MN, B_MN);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        for (int ks = 0; ks < p.k_steps; ++ks) {
+          uint64_t *ready = Cfg::kSplit ? &conv[stage] : &full[stage];
+          if (!mbar_wait_bounded(ready, phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
+          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
+#pragma unroll
+          for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+            const uint32_t a_off = A_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+            const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+            const uint32_t a_lbo = A_MN ? BK * 128 : 16;
+            const uint32_t b_lbo = B_MN ? BK * 128 : 16;
+            const uint64_t adesc = make_sw128_desc(a_base + a_off, a_lbo, 1024);
+            const uint64_t bdesc = make_sw128_desc(b_base + b_off, b_lbo, 1024);
+            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
+            if (KIND == kKindBF16) {
+              umma_f16(d_tmem, adesc, bdesc, idesc, accum);
+            } else if (KIND == kKindTF32) {
+              umma_tf32(d_tmem, adesc, bdesc, idesc, accum);
+            } else {
+              const uint32_t alo_base = smem_u32(sAlo + stage * Cfg::kABytes);
+              const uint32_t blo_base = smem_u32(sBlo + stage * Cfg::kBBytes);
+              const uint64_t alo = make_sw128_desc(alo_base + a_off, a_lbo, 1024);
+              const uint64_t blo = make_sw128_desc(blo_base + b_off, b_lbo, 1024);
+              umma_tf32(d_tmem, alo, bdesc, idesc, accum);  // small terms first
+              umma_tf32(d_tmem, adesc, blo, idesc, 1u);
+              umma_tf32(d_tmem, adesc, bdesc, idesc, 1u);
+            }
+          }
+          umma_commit(&empty[stage]);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit(&tfull[acc]);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      if (!ok) {
+        if (!*abort_flag) record_error(p.err, kErrTimeoutMma);
+        *abort_flag = 1;
+      }
+    }
+  } else if (warp < 6) {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+      TileCoord c = decode_tile(p, t);
+      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) {
+        if (!*abort_flag) record_error(p.err, kErrTimeoutEpilogue);
+        *abort_flag = 1;
+        break;
+      }
+      tc_fence_after();
+      const int64_t m = c.mt * BM + row;
+      const bool mval = m < p.m_size;
+      int64_t ob = m * p.so_m, ab = m * p.sa_m;
+#pragma unroll
+      for (int i = 0; i < kMaxTileLoops; ++i) {
+        ob += c.l[i] * p.loop_so[i];
+        ab += c.l[i] * p.loop_sa[i];
+      }
+      const int64_t n0 = c.nt * BN;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
+        tmem_ld_wait();
+        if (mval) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            const int64_t n = n0 + ch * 32 + j;
+            if (n < p.n_size) {
+              float x = __uint_as_float(v[j]);
+              const int64_t o = ob + n * p.so_n;
+              const int64_t a = ab + n * p.sa_n;
+              if (p.first_touch == 3 /*COPY*/) x += aux[a];
+              else if (p.first_touch == 2 /*ADD*/) x += out[o] + aux[a];
+              else if (p.first_touch != 0 /*not ZERO*/) x += out[o];
+              if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
+              else if (p.last_touch == 2 /*ADD*/) x += aux[a];
+              out[o] = x;
+            }
+          }
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  } else if (Cfg::kSplit) {
+    // ------------------------------------------------------------ hi/lo split
+    const int ct = threadIdx.x - 192;  // 0..127
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+      for (int ks = 0; ks < p.k_steps; ++ks) {
+        if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
+        float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
+#pragma unroll 4
+        for (int i = ct; i < Cfg::kABytes / 16; i += 128) {
+          float4 x = a[i];
+          float4 h, l;
+          h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
+          h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
+          h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
+          h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
+          a[i] = h;
+          alo[i] = l;
+        }
+        float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
+        float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+#pragma unroll 4
+        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) {
+          float4 x = b[i];
+          float4 h, l;
+          h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
+          h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
+          h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
+          h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
+          b[i] = h;
+          blo[i] = l;
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&conv[stage]);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok) {
+      if (!*abort_flag) record_error(p.err, kErrTimeoutConvert);
+      *abort_flag = 1;
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+template <int KIND, int BN, bool A_MN, bool B_MN>
+static cudaError_t launch_tc_t(CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
+                               float const *aux, float *out, int num_sms, cudaStream_t st) {
+  using Cfg = TcConfig<KIND, BN>;
+  auto kern = tc_contract_kernel<KIND, BN, A_MN, B_MN>;
+  static unsigned attr_set_mask = 0;  // one bit per device (attribute is per device)
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev >= 32 || !(attr_set_mask & (1u << dev))) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    if (dev < 32) attr_set_mask |= (1u << dev);
+  }
+  int64_t grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
+  if (grid < 1) return cudaSuccess;
+  kern<<<(unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ma, mb, p, aux, out);
+  return cudaGetLastError();
+}
+
+template <int KIND, int BN>
+static cudaError_t launch_tc_major(bool a_mn, bool b_mn, CUtensorMap const &ma,
+                                   CUtensorMap const &mb, TcParams const &p, float const *aux,
+                                   float *out, int num_sms, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_tc_t<KIND, BN, false, false>(ma, mb, p, aux, out, num_sms, st);
+  if (!a_mn && b_mn) return launch_tc_t<KIND, BN, false, true>(ma, mb, p, aux, out, num_sms, st);
+  if (a_mn && !b_mn) return launch_tc_t<KIND, BN, true, false>(ma, mb, p, aux, out, num_sms, st);
+  return launch_tc_t<KIND, BN, true, true>(ma, mb, p, aux, out, num_sms, st);
+}
+
+cudaError_t launch_tc_contract(int kind, int bn, bool a_mn, bool b_mn, CUtensorMap const &ma,
+                               CUtensorMap const &mb, TcParams const &p, float const *aux,
+                               float *out, int num_sms, cudaStream_t st) {
+  if (kind == kKindBF16 && bn == 256)
+    return launch_tc_major<kKindBF16, 256>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindBF16 && bn == 128)
+    return launch_tc_major<kKindBF16, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 256)
+    return launch_tc_major<kKindTF32, 256>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 128)
+    return launch_tc_major<kKindTF32, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKind3xTF32 && bn == 128)
+    return launch_tc_major<kKind3xTF32, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  return cudaErrorInvalidValue;
+}
+
+int tc_block_k(int kind) { return kind == kKindBF16 ? 64 : 32; }
+
+}  // namespace eir
