@@ -31,6 +31,7 @@ EXPORTS = [
     "eir_expression_eval", "eir_expression_num_ops", "eir_expression_num_tensors",
     "eir_expression_tensor_dims", "eir_expression_destroy", "eir_expression_describe",
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
+    "eir_plan_profile", "eir_plan_profile_read",
 ]
 
 
@@ -80,6 +81,8 @@ def lib() -> ctypes.CDLL:
         L.eir_last_error_string.restype = c_char_p
         L.eir_check_device_errors.argtypes = [c_void_p]
         L.eir_launch_count.restype = c_int64
+        L.eir_plan_profile.argtypes = [c_void_p, c_int32]
+        L.eir_plan_profile_read.argtypes = [c_void_p, POINTER(ctypes.c_double), POINTER(c_int64)]
         if hasattr(L, "eir_expression_create"):
             L.eir_expression_create.argtypes = [c_char_p, c_char_p, c_char_p, c_int32, c_int32,
                                                  POINTER(c_void_p)]
@@ -136,6 +139,16 @@ class Plan:
 
     def describe(self) -> str:
         return lib().eir_plan_describe(self._h).decode()
+
+    def profile(self, enable: bool = True) -> None:
+        check(lib().eir_plan_profile(self._h, 1 if enable else 0))
+
+    def profile_read(self) -> tuple:
+        """(summed main-kernel milliseconds, timed launches) since the last read."""
+        ms = ctypes.c_double()
+        n = c_int64()
+        check(lib().eir_plan_profile_read(self._h, ctypes.byref(ms), ctypes.byref(n)))
+        return float(ms.value), int(n.value)
 
     def close(self) -> None:
         if self._h:

@@ -96,7 +96,7 @@ int encode_map(eir::MapSpec const &s, void const *ptr, CUtensorMap *m) {
   if (rc != EIR_SUCCESS) return rc;
   uint32_t estr[5] = {1, 1, 1, 1, 1};
   CUresult r = g_encode(m, s.dtype, s.rank, const_cast<void *>(ptr), s.dims, s.strides_bytes, s.box,
-                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        estr, CU_TENSOR_MAP_INTERLEAVE_NONE, s.swizzle,
                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS)
     return set_error(EIR_CUDA_ERROR, "cuTensorMapEncodeTiled failed (" + std::to_string((int)r) + ")");
@@ -446,11 +446,15 @@ bool try_tc(eir_plan *p, std::string *why) {
     double c128 = (double)ceil_div(t128, num_sms) * (128 + 32);
     double c256 = (double)ceil_div(t256, num_sms) * (256 + 32);
     bn = (d[np].size > 128 && c256 <= c128) ? 256 : 128;
+    int64_t force = env_int("EIR_TC_BN", 0);  // tuning override: 128 or 256
+    if (force == 128 || force == 256) bn = (int)force;
   }
 
   // TMA maps
   auto fill_map = [&](eir::MapSpec &ms, bool left, bool mn, int rowdim, int rows) -> bool {
     ms.dtype = (kind == 0) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    // 32-bit MN-major operands: the only tcgen05 layout is 128B swizzle with 32B atoms
+    ms.swizzle = (mn && esize == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
     auto st = [&](int i) { return left ? sl_of(i) : sr_of(i); };
     int first = mn ? rowdim : kp, second = mn ? kp : rowdim;
     if (st(first) != 1) return false;
@@ -583,8 +587,35 @@ bool valid_last(int k) {
   return k == EIR_KTYPE_RELU || k == EIR_KTYPE_ADD || k == EIR_KTYPE_UNDEFINED;
 }
 
+// events around a plan's main kernel when profiling is enabled
+struct ProfScope {
+  eir_plan *p;
+  cudaStream_t st;
+  cudaEvent_t e1 = nullptr;
+  ProfScope(eir_plan *plan, cudaStream_t s) : p(plan), st(s) {
+    if (!p->profile) return;
+    if (p->prof_used == p->prof_events.size()) {
+      cudaEvent_t a, b;
+      if (cudaEventCreate(&a) != cudaSuccess) return;
+      if (cudaEventCreate(&b) != cudaSuccess) {
+        cudaEventDestroy(a);
+        return;
+      }
+      p->prof_events.emplace_back(a, b);
+    }
+    cudaEventRecord(p->prof_events[p->prof_used].first, st);
+    e1 = p->prof_events[p->prof_used].second;
+  }
+  ~ProfScope() {
+    if (e1 == nullptr) return;
+    cudaEventRecord(e1, st);
+    p->prof_used++;
+  }
+};
+
 int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
              cudaStream_t st) {
+  ProfScope prof(p, st);
   cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt, l, r, aux, out, st);
   if (e != cudaSuccess) return cuda_fail(e, "simt contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
@@ -747,6 +778,7 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   }
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
+  ProfScope prof(p, st);
   cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->a_mn, p->b_mn, ma, mb, tp,
                                           static_cast<float const *>(aux), static_cast<float *>(out),
                                           ds->num_sms, st);
@@ -789,6 +821,7 @@ int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
   if (pp.mode == 0 && pp.vec > 1 &&
       ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % (pp.vec * p->esize)))
     pp.vec = 1;
+  ProfScope prof(p, static_cast<cudaStream_t>(stream));
   cudaError_t e = eir::launch_permute(p->esize, pp, in, out, ds->num_sms,
                                       static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "permute launch");
@@ -796,8 +829,35 @@ int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
   return EIR_SUCCESS;
 }
 
+int eir_plan_profile(eir_plan *p, int32_t enable) {
+  if (p == nullptr) return set_error(EIR_INVALID_ARGUMENT, "null plan");
+  p->profile = enable != 0;
+  return EIR_SUCCESS;
+}
+
+int eir_plan_profile_read(eir_plan *p, double *ms_total, int64_t *launches) {
+  if (p == nullptr) return set_error(EIR_INVALID_ARGUMENT, "null plan");
+  double tot = 0.0;
+  for (size_t i = 0; i < p->prof_used; ++i) {
+    cudaError_t e = cudaEventSynchronize(p->prof_events[i].second);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventSynchronize");
+    float ms = 0.f;
+    e = cudaEventElapsedTime(&ms, p->prof_events[i].first, p->prof_events[i].second);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventElapsedTime");
+    tot += ms;
+  }
+  if (ms_total) *ms_total = tot;
+  if (launches) *launches = (int64_t)p->prof_used;
+  p->prof_used = 0;
+  return EIR_SUCCESS;
+}
+
 int eir_plan_destroy(eir_plan *p) {
   if (p == nullptr) return EIR_SUCCESS;
+  for (auto &ev : p->prof_events) {
+    cudaEventDestroy(ev.first);
+    cudaEventDestroy(ev.second);
+  }
   if (p->pre) eir_plan_destroy(p->pre);
   if (p->ws) {
     int cur = 0;

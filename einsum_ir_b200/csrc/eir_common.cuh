@@ -161,16 +161,20 @@ __device__ __forceinline__ void tmem_ld_wait() {
   asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
 }
 
+// tcgen05 shared-memory layout types (descriptor bits 61..63)
+constexpr uint32_t kLayoutSw128 = 2;        // 128B swizzle, 16-byte atoms
+constexpr uint32_t kLayoutSw128Base32 = 1;  // 128B swizzle, 32-byte atoms (32-bit MN-major)
+
 // Shared-memory matrix descriptor for tcgen05 (sm_100 "version 1" format):
-// start address, leading/stride byte offsets (16-byte units), 128B swizzle.
-__device__ __forceinline__ uint64_t make_sw128_desc(uint32_t saddr, uint32_t lbo_bytes,
-                                                    uint32_t sbo_bytes) {
+// start address, leading/stride byte offsets (16-byte units), layout type.
+__device__ __forceinline__ uint64_t make_smem_desc(uint32_t saddr, uint32_t lbo_bytes,
+                                                   uint32_t sbo_bytes, uint32_t layout) {
   uint64_t d = 0;
   d |= static_cast<uint64_t>((saddr >> 4) & 0x3FFFu);
   d |= static_cast<uint64_t>((lbo_bytes >> 4) & 0x3FFFu) << 16;
   d |= static_cast<uint64_t>((sbo_bytes >> 4) & 0x3FFFu) << 32;
   d |= 1ull << 46;  // descriptor version for sm_100
-  d |= 2ull << 61;  // SWIZZLE_128B
+  d |= static_cast<uint64_t>(layout & 7u) << 61;
   return d;
 }
 

@@ -8,7 +8,7 @@
 #include <string>
 #include <vector>
 #include "eir_params.h"
-#include "../../include/eir_cuda.h"
+#include "eir_cuda.h"
 
 namespace eir {
 
@@ -26,6 +26,7 @@ struct MapSpec {
   uint64_t strides_bytes[4] = {16, 16, 16, 16};  // strides of dims 1..4
   uint32_t box[5] = {1, 1, 1, 1, 1};
   CUtensorMapDataType dtype = CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+  CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B;
 };
 
 struct TensorMapCache {
@@ -66,4 +67,9 @@ struct eir_plan {
   // ---- permute
   eir::PermuteParams perm;
   int esize = 4;
+
+  // ---- main-kernel timing (eir_plan_profile)
+  bool profile = false;
+  std::vector<std::pair<cudaEvent_t, cudaEvent_t>> prof_events;
+  size_t prof_used = 0;
 };

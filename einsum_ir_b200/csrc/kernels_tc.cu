@@ -92,6 +92,16 @@ __device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, T
   }
 }
 
+// Start offset of a tile's K-step walk. Tiles running at the same time start at
+// different K steps so they do not all fetch the same operand lines from L2 at
+// once (the sum over K is order independent up to FP32 rounding). Producer and
+// MMA issuer only need to agree on the order; the first MMA of the walk always
+// initialises the accumulator.
+__device__ __forceinline__ int k_rotation(TcParams const &p, int64_t t) {
+  if (p.k_steps <= 1) return 0;
+  return (int)((t * 7) % p.k_steps);
+}
+
 __device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
   uint32_t r;
   asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
@@ -157,7 +167,10 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
       uint32_t phase = 0;
       for (int64_t t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
         TileCoord c = decode_tile(p, t);
-        for (int ks = 0; ks < p.k_steps; ++ks) {
+        const int kshift = k_rotation(p, t);
+        for (int ks0 = 0; ks0 < p.k_steps; ++ks0) {
+          int ks = ks0 + kshift;
+          if (ks >= p.k_steps) ks -= p.k_steps;
           int kp = ks % p.kp_blocks;
           int64_t r = ks / p.kp_blocks;
           int64_t ko0 = r % p.ko_size[0];
@@ -227,10 +240,15 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
           for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
             const uint32_t a_off = A_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
             const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+            // MN-major 32-bit operands use the 32-byte-atom swizzle (4-row K groups)
+            constexpr bool kA32 = A_MN && Cfg::kEsize == 4, kB32 = B_MN && Cfg::kEsize == 4;
+            constexpr uint32_t a_lay = kA32 ? kLayoutSw128Base32 : kLayoutSw128;
+            constexpr uint32_t b_lay = kB32 ? kLayoutSw128Base32 : kLayoutSw128;
+            constexpr uint32_t a_sbo = kA32 ? 512 : 1024, b_sbo = kB32 ? 512 : 1024;
             const uint32_t a_lbo = A_MN ? BK * 128 : 16;
             const uint32_t b_lbo = B_MN ? BK * 128 : 16;
-            const uint64_t adesc = make_sw128_desc(a_base + a_off, a_lbo, 1024);
-            const uint64_t bdesc = make_sw128_desc(b_base + b_off, b_lbo, 1024);
+            const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
+            const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
             const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
             if (KIND == kKindBF16) {
               umma_f16(d_tmem, adesc, bdesc, idesc, accum);
@@ -239,8 +257,8 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
             } else {
               const uint32_t alo_base = smem_u32(sAlo + stage * Cfg::kABytes);
               const uint32_t blo_base = smem_u32(sBlo + stage * Cfg::kBBytes);
-              const uint64_t alo = make_sw128_desc(alo_base + a_off, a_lbo, 1024);
-              const uint64_t blo = make_sw128_desc(blo_base + b_off, b_lbo, 1024);
+              const uint64_t alo = make_smem_desc(alo_base + a_off, a_lbo, a_sbo, a_lay);
+              const uint64_t blo = make_smem_desc(blo_base + b_off, b_lbo, b_sbo, b_lay);
               umma_tf32(d_tmem, alo, bdesc, idesc, accum);  // small terms first
               umma_tf32(d_tmem, adesc, blo, idesc, 1u);
               umma_tf32(d_tmem, adesc, bdesc, idesc, 1u);

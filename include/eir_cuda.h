@@ -154,6 +154,14 @@ int     eir_expression_tensor_dims(eir_expression const *expr, int32_t tensor,
 int     eir_expression_destroy(eir_expression *expr);
 char const *eir_expression_describe(eir_expression const *expr);
 
+/* --- kernel timing (diagnostics) ------------------------------------------ */
+/* enable: record CUDA events around the plan's main kernel on every call
+ * (the pre-permute of a workspace operand is not included) */
+int     eir_plan_profile(eir_plan *plan, int32_t enable);
+/* synchronizes on the recorded events, returns the summed main-kernel time in
+ * milliseconds and the number of timed launches, then clears the record */
+int     eir_plan_profile_read(eir_plan *plan, double *ms_total, int64_t *launches);
+
 /* --- errors / diagnostics ----------------------------------------------- */
 char const *eir_last_error_string(void);
 /* reads and clears the device-side error word of the current device

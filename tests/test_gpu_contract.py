@@ -99,8 +99,8 @@ TC_CASES = [
     ("km,nk->nm", dict(m=256, n=384, k=192), "bf16"),      # A MN-major, B K-major
     ("mk,kn->nm", dict(m=256, n=384, k=192), "bf16"),      # A K-major, B MN-major
     ("km,kn->nm", dict(m=256, n=384, k=192), "bf16"),      # both MN-major
-    ("mk,nk->nm", dict(m=130, n=70, k=33), "bf16"),        # ragged tails
-    ("km,kn->nm", dict(m=130, n=70, k=33), "fp32"),
+    ("mk,nk->nm", dict(m=130, n=70, k=40), "bf16"),        # ragged tails
+    ("km,kn->nm", dict(m=132, n=72, k=33), "fp32"),
     ("mk,nk->nm", dict(m=256, n=256, k=160), "fp32"),
     ("km,nk->nm", dict(m=256, n=256, k=160), "tf32"),
     ("km,kn->nm", dict(m=192, n=320, k=96), "tf32"),
@@ -111,7 +111,7 @@ TC_CASES = [
     # non-fusable M dims and C dims inside, tile loops + outer K loops
     ("axmk,nkx->anm", dict(a=3, x=2, m=96, k=64, n=80), "bf16"),
     ("cmk,cnk->cnm", dict(c=3, m=128, n=192, k=128), "fp32"),
-    ("abmkq,cnqk->abcnm", dict(a=2, b=2, c=2, m=64, n=64, k=32, q=3), "bf16"),
+    ("abmkq,cnqk->acbnm", dict(a=2, b=3, c=2, m=64, n=48, k=16, q=8), "bf16"),
 ]
 
 
@@ -150,6 +150,7 @@ SIMT_CASES = [
     ("mk,nk->nm", dict(m=67, n=45, k=29), "fp64"),
     ("km,kn->nm", dict(m=67, n=45, k=29), "bf16"),
     ("cmk,cnk->cnm", dict(c=3, m=17, n=19, k=23), "fp32"),
+    ("abmkq,cnqk->abcnm", dict(a=2, b=2, c=2, m=64, n=64, k=32, q=3), "bf16"),
 ]
 
 
