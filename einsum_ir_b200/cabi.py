@@ -31,7 +31,7 @@ EXPORTS = [
     "eir_expression_eval", "eir_expression_num_ops", "eir_expression_num_tensors",
     "eir_expression_tensor_dims", "eir_expression_destroy", "eir_expression_describe",
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
-    "eir_plan_profile", "eir_plan_profile_read",
+    "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc",
 ]
 
 
@@ -67,6 +67,7 @@ def lib() -> ctypes.CDLL:
         L = ctypes.CDLL(str(LIB_PATH))
         L.eir_contract_plan_create.argtypes = [POINTER(EirContractDesc), POINTER(c_void_p)]
         L.eir_contract.argtypes = [c_void_p] * 6
+        L.eir_contract_no_alloc.argtypes = [c_void_p] * 6
         L.eir_contract_num_ops.argtypes = [c_void_p]
         L.eir_contract_num_ops.restype = c_int64
         L.eir_permute_plan_create.argtypes = [c_int32, POINTER(c_int64), POINTER(c_int64),
@@ -186,6 +187,11 @@ class ContractPlan(Plan):
     def contract(self, left, right, out, aux=None, stream: int = 0) -> None:
         check(lib().eir_contract(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
                                  c_void_p(stream)))
+
+    def contract_no_alloc(self, left, right, out, aux=None, stream: int = 0) -> None:
+        """eir_contract_no_alloc: same result, scratch from the library's static array."""
+        check(lib().eir_contract_no_alloc(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
+                                          c_void_p(stream)))
 
 
 class PermutePlan(Plan):

@@ -624,6 +624,14 @@ int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *o
 
 }  // namespace
 
+// library-internal helpers shared with other translation units (eir_plan.h)
+namespace eir {
+int api_set_error(int code, char const *msg) { return set_error(code, msg); }
+int api_cuda_fail(cudaError_t e, char const *where) { return cuda_fail(e, where); }
+int api_encode_map(MapSpec const &s, void const *ptr, CUtensorMap *m) { return encode_map(s, ptr, m); }
+void api_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+}  // namespace eir
+
 // =================================================================== C-ABI
 extern "C" {
 

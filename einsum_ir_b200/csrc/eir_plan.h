@@ -34,6 +34,12 @@ struct TensorMapCache {
   CUtensorMap map;
 };
 
+// helpers defined in eir_capi.cu
+int api_set_error(int code, char const *msg);
+int api_cuda_fail(cudaError_t e, char const *where);
+int api_encode_map(MapSpec const &s, void const *ptr, CUtensorMap *m);
+void api_count_launch();
+
 }  // namespace eir
 
 struct eir_plan {

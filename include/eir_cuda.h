@@ -122,6 +122,17 @@ int     eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan)
 int     eir_contract(eir_plan *plan, void const *left, void const *right,
                      void const *out_aux, void *out, void *stream);
 int64_t eir_contract_num_ops(eir_plan const *plan);
+/* Same contraction as eir_contract, but allocates no device memory: for
+ * callers whose device memory is owned by another allocator (a framework's
+ * caching allocator, a serving arena) or that cannot afford cudaMalloc's
+ * synchronisation on the hot path. A plan's pre-permute scratch comes from a
+ * static 8 MiB array in the library's device image (held on every GPU that
+ * loads the library); plans needing more are rejected with
+ * EIR_INVALID_ARGUMENT. The first call on a device does a one-time set-up
+ * (make it before any stream capture). All calls share the array: calls that
+ * overlap on the GPU race. No counterpart in the reference. */
+int     eir_contract_no_alloc(eir_plan *plan, void const *left, void const *right,
+                              void const *out_aux, void *out, void *stream);
 
 /* --- unary permute (copy with reordered strides) ------------------------- */
 /* sizes/strides are per dimension, in elements; any order */

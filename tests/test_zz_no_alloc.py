@@ -1,0 +1,60 @@
+"""eir_contract_no_alloc against eir_contract (GPU, through the C-ABI).
+
+The no-allocation entry point exists for callers that may not call cudaMalloc
+(their device memory belongs to another allocator, or the allocation's
+synchronisation is not acceptable on their hot path). It must give the same
+result as the allocating entry point. This file is collected last so that a
+run stopping at the first failure has already run every other test, and it
+works both alone in a fresh process and after the rest of the suite.
+"""
+import numpy as np
+import pytest
+
+from einsum_ir_b200 import binary, cabi
+from tests import _oracle
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-5  # relative Frobenius error, as for the BF16 contraction tests
+
+
+def _plan(expr, sizes):
+    il, ir, io, names = binary.parse_binary(expr)
+    sz = {i: sizes[c] for i, c in enumerate(names)}
+    dims = binary.contraction_dims(il, ir, io, sz)
+    shapes = ([sz[i] for i in il], [sz[i] for i in ir], [sz[i] for i in io])
+    return cabi.ContractPlan(dims, cabi.BF16, cabi.BF16, cabi.FP32), shapes
+
+
+def test_no_alloc_matches_contract(cuda, monkeypatch):
+    import torch
+    monkeypatch.setenv("EIR_TC_MIN_OPS", "0")
+    # BASELINE config 2 at reduced a: tensor-core path with a pre-permuted right operand
+    plan, (sl, sr, so) = _plan("akmj,njk->anm", dict(a=2, k=8, m=256, j=64, n=256))
+    assert plan.family == cabi.FAMILY_TC and plan.workspace_bytes > 0, plan.describe()
+    g = torch.Generator().manual_seed(11)
+    for call in range(2):  # two calls in a row: the shared scratch is reused
+        l = ((torch.rand(sl, generator=g) * 2 - 1).to(torch.bfloat16)).to(cuda)
+        r = ((torch.rand(sr, generator=g) * 2 - 1).to(torch.bfloat16)).to(cuda)
+        want = torch.full(so, float("nan"), device=cuda)
+        got = torch.full(so, float("nan"), device=cuda)
+        plan.contract(l, r, want)
+        plan.contract_no_alloc(l, r, got)
+        torch.cuda.synchronize()
+        err = _oracle.rel_err(got.cpu().numpy(), want.cpu().numpy())
+        assert np.isfinite(got.cpu().numpy()).all()
+        assert err <= TOL, f"call {call}: rel err {err:.3e}"
+
+
+def test_no_alloc_rejects_oversized_scratch(cuda):
+    import torch
+    # the pre-permuted (smaller) operand is the right one: 512*64*256 BF16 = 16 MiB,
+    # more than the 8 MiB static scratch (left: 256*1024*64 BF16 = 32 MiB)
+    plan, (sl, sr, so) = _plan("akmj,njk->anm", dict(a=1, k=256, m=1024, j=64, n=512))
+    assert plan.workspace_bytes > 8 * 2 ** 20, plan.describe()
+    l = torch.zeros(sl, dtype=torch.bfloat16, device=cuda)
+    r = torch.zeros(sr, dtype=torch.bfloat16, device=cuda)
+    out = torch.zeros(so, device=cuda)
+    with pytest.raises(cabi.EirError) as ei:
+        plan.contract_no_alloc(l, r, out)
+    assert ei.value.code == 52 and "static scratch" in str(ei.value)
