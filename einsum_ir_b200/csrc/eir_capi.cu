@@ -536,6 +536,12 @@ bool try_tc(eir_plan *p, std::string *why) {
   for (int j = 0; j < t.n_loops; ++j) t.total_tiles *= t.loop_size[j];
   t.first_touch = p->first;
   t.last_touch = p->last;
+  t.group_m = (int32_t)std::max<int64_t>(1, env_int("EIR_TC_GROUP_M", 16));
+  // K blocks per ring stage: two (larger stages) whenever there are at least two K blocks
+  int ksub = (kind != 2 && t.k_steps >= 2) ? 2 : 1;
+  int64_t force_ksub = env_int("EIR_TC_KSUB", 0);  // tuning override: 1 or 2
+  if (kind != 2 && (force_ksub == 1 || force_ksub == 2)) ksub = (int)force_ksub;
+  p->tc_ksub = ksub;
 
   p->tc = true;
   p->tc_kind = kind;
@@ -569,9 +575,9 @@ bool try_tc(eir_plan *p, std::string *why) {
 
   char buf[512];
   std::snprintf(buf, sizeof(buf),
-                "tc kind=%s BN=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d tiles=%lld "
-                "ksteps=%d prepack=%s",
-                kind == 0 ? "bf16" : (kind == 1 ? "tf32" : "3xtf32"), bn, a_mn ? "MN" : "K",
+                "tc kind=%s BN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
+                "tiles=%lld ksteps=%d prepack=%s",
+                kind == 0 ? "bf16" : (kind == 1 ? "tf32" : "3xtf32"), bn, p->tc_ksub, a_mn ? "MN" : "K",
                 b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
                 (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
                 (long long)t.total_tiles, t.k_steps,
@@ -787,7 +793,7 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
   ProfScope prof(p, st);
-  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->a_mn, p->b_mn, ma, mb, tp,
+  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
                                           static_cast<float const *>(aux), static_cast<float *>(out),
                                           ds->num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");

@@ -76,6 +76,33 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// Bounded wait for a whole warp that is not on the latency-critical path (the
+// epilogue waiting for an accumulator, the TF32 splitter waiting for a stage):
+// only lane 0 polls the barrier, with a short sleep between polls, while the
+// other lanes wait at __syncwarp. Many threads polling an mbarrier in a tight
+// loop slow down the TMA transactions that complete on the same barrier unit.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, volatile int *abort) {
+  int ok = 1;
+  if ((threadIdx.x & 31) == 0) {
+    if (!mbar_try_wait(bar, parity)) {
+      long long t0 = clock64();
+      while (true) {
+        __nanosleep(128);
+        if (mbar_try_wait(bar, parity)) break;
+        if (*abort || clock64() - t0 > kWaitTimeoutCycles) {
+          ok = 0;
+          break;
+        }
+      }
+    }
+  }
+  ok = __shfl_sync(0xffffffffu, ok, 0);
+  __syncwarp();
+  // every lane observes the completed phase itself (acquire); it is complete already
+  if (ok) (void)mbar_try_wait(bar, parity);
+  return ok != 0;
+}
+
 __device__ __forceinline__ void record_error(uint32_t *err, uint32_t code) {
   if (err != nullptr) atomicCAS(err, 0u, code);
 }

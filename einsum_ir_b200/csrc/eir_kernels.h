@@ -14,9 +14,10 @@ cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, vo
                            int num_sms, cudaStream_t st);
 
 // kind: 0 = BF16 (kind::f16), 1 = TF32, 2 = 3xTF32 (FP32-accurate)
-cudaError_t launch_tc_contract(int kind, int bn, bool a_mn, bool b_mn, CUtensorMap const &ma,
-                               CUtensorMap const &mb, TcParams const &p, float const *aux,
-                               float *out, int num_sms, cudaStream_t st);
+// ksub: K blocks (128-byte swizzle rows) per ring stage, 1 or 2
+cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
+                               CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
+                               float const *aux, float *out, int num_sms, cudaStream_t st);
 
 int tc_block_k(int kind);
 

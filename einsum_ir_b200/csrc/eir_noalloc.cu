@@ -148,7 +148,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   }
   eir::TcParams tp = p->tcp;
   tp.err = reinterpret_cast<uint32_t *>(d->scratch);  // header word
-  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->a_mn, p->b_mn, ma, mb, tp,
+  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
                                           static_cast<float const *>(aux), static_cast<float *>(out),
                                           d->num_sms, st);
   if (e != cudaSuccess) return eir::api_cuda_fail(e, "tc contraction launch");

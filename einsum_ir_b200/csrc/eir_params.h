@@ -65,6 +65,7 @@ struct TcParams {
   int64_t total_tiles;
   int32_t m_tiles, n_tiles, kp_blocks, k_steps;
   int32_t n_loops;
+  int32_t group_m;                          // M tiles per raster group
   int32_t first_touch, last_touch;
   int8_t a_src[5];
   int8_t b_src[5];

@@ -55,7 +55,7 @@ struct eir_plan {
   std::vector<eir::LDim> dims;   // after size-1 removal and fusion
   eir::SimtParams simt;
   bool tc = false;
-  int tc_kind = 0, tc_bn = 128;
+  int tc_kind = 0, tc_bn = 128, tc_ksub = 1;
   bool a_mn = false, b_mn = false;
   eir::TcParams tcp{};
   eir::MapSpec map_a, map_b;

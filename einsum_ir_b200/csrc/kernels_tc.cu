@@ -2,19 +2,25 @@
 //
 // One persistent CTA per SM walks output tiles of 128 (primitive M) x BN
 // (primitive N). The remaining C / M / N dims are "tile loops" (scheduler
-// coordinates); the K range is the primitive K dim (blocked by BK) times up
-// to two outer K dims. Operands are read in their native strided layouts by
-// 5-D TMA tensor maps (128B swizzle, K-major or MN-major per operand), staged
-// in a shared-memory ring and consumed by tcgen05.mma issued from one thread,
-// with the FP32 accumulator in TMEM (double buffered, so the epilogue of one
-// tile overlaps the main loop of the next).
+// coordinates); the K range is the primitive K dim (in blocks of one 128-byte
+// swizzle row) times up to two outer K dims. Operands are read in their native
+// strided layouts by 5-D TMA tensor maps (128B swizzle, K-major or MN-major
+// per operand), staged in a shared-memory ring and consumed by tcgen05.mma
+// issued from one thread, with the FP32 accumulator in TMEM (double buffered,
+// so the epilogue of one tile overlaps the main loop of the next).
+//
+// A ring stage holds KSUB consecutive K blocks of both operands. The TMA
+// producer / MMA consumer handshake costs a roughly fixed time per stage, so
+// larger stages (KSUB = 2) raise the operand rate per SM. Tiles are walked in
+// groups of `group_m` M tiles so CTAs running at the same time share operand
+// tiles in L2.
 //
 // Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+TMEM owner),
 // warps 2..5 = epilogue (TMEM -> registers -> global, fused first/last touch:
 // ZERO/COPY/ADD before, RELU/ADD after, aux read through broadcast strides),
 // warps 6..9 (3xTF32 only) = split each staged FP32 tile into hi + lo TF32
 // parts in shared memory (hi = round-to-nearest TF32, lo = x - hi) so three
-// MMAs (hi*hi + hi*lo + lo*hi) give an FP32-accurate product.
+// MMAs (lo*hi + hi*lo + hi*hi) give an FP32-accurate product.
 //
 // Semantics follow the reference loop engine: first touch at the first K
 // step, last touch after the last (ContractionBackend.cpp:296-348,495-515;
@@ -28,22 +34,25 @@ namespace eir {
 
 enum { kKindBF16 = 0, kKindTF32 = 1, kKind3xTF32 = 2 };
 
-template <int KIND, int BN>
+template <int KIND, int BN, int KSUB>
 struct TcConfig {
   static constexpr int kEsize = (KIND == kKindBF16) ? 2 : 4;
   static constexpr int kBM = 128;
-  static constexpr int kBK = 128 / kEsize;                 // one 128-byte swizzle row of K
+  static constexpr int kBK = 128 / kEsize;                 // K elements of one 128-byte swizzle row
   static constexpr int kMmaK = (KIND == kKindBF16) ? 16 : 8;
   static constexpr int kRowsPerBox = 128 / kEsize;         // MN-major: rows per 128B box
-  static constexpr int kABytes = kBM * 128;
-  static constexpr int kBBytes = BN * 128;
+  static constexpr int kASub = kBM * 128;                  // A bytes of one K block
+  static constexpr int kBSub = BN * 128;                   // B bytes of one K block
+  static constexpr int kABytes = KSUB * kASub;             // per stage
+  static constexpr int kBBytes = KSUB * kBSub;
   static constexpr bool kSplit = (KIND == kKind3xTF32);
   static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
-  static constexpr int kStages = (KIND == kKind3xTF32) ? 3 : (196608 / kStageBytes);
+  static constexpr int kStages = 196608 / kStageBytes;
   static constexpr int kThreads = kSplit ? 320 : 192;
   static constexpr int kTmemCols = 2 * BN;                 // double-buffered accumulator
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
+  static_assert(kStages >= 2, "at least two ring stages");
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
@@ -62,12 +71,20 @@ struct TileCoord {
   int64_t l[kMaxTileLoops];
 };
 
+// tile index -> (M tile, N tile, tile-loop indices); M/N tiles in groups of group_m M tiles
 __device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
   TileCoord c;
-  c.mt = t % p.m_tiles;
-  t /= p.m_tiles;
-  c.nt = t % p.n_tiles;
-  t /= p.n_tiles;
+  const int64_t mn = (int64_t)p.m_tiles * p.n_tiles;
+  int64_t u = t % mn;
+  t /= mn;
+  const int64_t gsz_full = (int64_t)p.group_m * p.n_tiles;
+  const int64_t g = u / gsz_full;
+  const int64_t first_m = g * p.group_m;
+  const int64_t rem_m = p.m_tiles - first_m;
+  const int64_t gm = rem_m < p.group_m ? rem_m : p.group_m;
+  const int64_t r = u - g * gsz_full;
+  c.mt = first_m + r % gm;
+  c.nt = r / gm;
 #pragma unroll
   for (int i = 0; i < kMaxTileLoops; ++i) {
     if (i < p.n_loops) {
@@ -92,14 +109,14 @@ __device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, T
   }
 }
 
-// Start offset of a tile's K-step walk. Tiles running at the same time start at
-// different K steps so they do not all fetch the same operand lines from L2 at
-// once (the sum over K is order independent up to FP32 rounding). Producer and
-// MMA issuer only need to agree on the order; the first MMA of the walk always
-// initialises the accumulator.
-__device__ __forceinline__ int k_rotation(TcParams const &p, int64_t t) {
-  if (p.k_steps <= 1) return 0;
-  return (int)((t * 7) % p.k_steps);
+// Start offset (in stages) of a tile's K walk. Tiles running at the same time
+// start at different K positions so they do not all fetch the same operand
+// lines at once (the sum over K is order independent up to FP32 rounding).
+// Producer and MMA issuer only need to agree on the order of stages; the first
+// MMA of a tile's walk always initialises the accumulator.
+__device__ __forceinline__ int k_rotation(int64_t t, int n_stages) {
+  if (n_stages <= 1) return 0;
+  return (int)((t * 7) % n_stages);
 }
 
 __device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
@@ -108,12 +125,22 @@ __device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
   return r;
 }
 
-template <int KIND, int BN, bool A_MN, bool B_MN>
-__global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
+__device__ __forceinline__ void split_tf32(float4 *hi_io, float4 *lo_out) {
+  float4 x = *hi_io, h, l;
+  h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
+  h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
+  h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
+  h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
+  *hi_io = h;
+  *lo_out = l;
+}
+
+template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
+__global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
     tc_contract_kernel(const __grid_constant__ CUtensorMap map_a,
                        const __grid_constant__ CUtensorMap map_b, const TcParams p,
                        const float *__restrict__ aux, float *__restrict__ out) {
-  using Cfg = TcConfig<KIND, BN>;
+  using Cfg = TcConfig<KIND, BN, KSUB>;
   constexpr int S = Cfg::kStages;
   constexpr int BK = Cfg::kBK;
   constexpr int BM = Cfg::kBM;
@@ -126,16 +153,18 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
   uint8_t *sAlo = sB + S * Cfg::kBBytes;               // (split) S x kABytes
   uint8_t *sBlo = sAlo + (Cfg::kSplit ? S * Cfg::kABytes : 0);
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
-  uint64_t *full = bars;            // S
-  uint64_t *empty = bars + S;       // S
-  uint64_t *conv = bars + 2 * S;    // S (split only)
-  uint64_t *tfull = bars + 3 * S;   // 2
+  uint64_t *full = bars;                // S
+  uint64_t *empty = bars + S;           // S
+  uint64_t *conv = bars + 2 * S;        // S (split only)
+  uint64_t *tfull = bars + 3 * S;       // 2
   uint64_t *tempty = bars + 3 * S + 2;  // 2
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 4);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
+  // K walk in stages of KSUB K blocks
+  const int n_kstages = (p.k_steps + KSUB - 1) / KSUB;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < S; ++s) {
@@ -167,42 +196,47 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
       uint32_t phase = 0;
       for (int64_t t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
         TileCoord c = decode_tile(p, t);
-        const int kshift = k_rotation(p, t);
-        for (int ks0 = 0; ks0 < p.k_steps; ++ks0) {
-          int ks = ks0 + kshift;
-          if (ks >= p.k_steps) ks -= p.k_steps;
-          int kp = ks % p.kp_blocks;
-          int64_t r = ks / p.kp_blocks;
-          int64_t ko0 = r % p.ko_size[0];
-          int64_t ko1 = r / p.ko_size[0];
+        const int rot = k_rotation(t, n_kstages);
+        const int mrow = (int)(c.mt * BM), nrow = (int)(c.nt * BN);
+        for (int js = 0; js < n_kstages; ++js) {
+          int ksg = js + rot;
+          if (ksg >= n_kstages) ksg -= n_kstages;
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
             if (!*abort_flag) record_error(p.err, kErrTimeoutProducer);
             *abort_flag = 1;
             break;
           }
-          mbar_arrive_expect_tx(&full[stage], Cfg::kABytes + Cfg::kBBytes);
-          int a2 = src_coord(p.a_src[2], ko0, ko1, c), a3 = src_coord(p.a_src[3], ko0, ko1, c),
-              a4 = src_coord(p.a_src[4], ko0, ko1, c);
-          int b2 = src_coord(p.b_src[2], ko0, ko1, c), b3 = src_coord(p.b_src[3], ko0, ko1, c),
-              b4 = src_coord(p.b_src[4], ko0, ko1, c);
-          uint8_t *dA = sA + stage * Cfg::kABytes;
-          uint8_t *dB = sB + stage * Cfg::kBBytes;
-          int mrow = (int)(c.mt * BM), nrow = (int)(c.nt * BN), kcol = kp * BK;
-          if (!A_MN) {
-            tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
-          } else {
+          const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
+          mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
+          for (int sub = 0; sub < nsub; ++sub) {
+            const int ks = ksg * KSUB + sub;
+            const int kp = ks % p.kp_blocks;
+            const int64_t r = ks / p.kp_blocks;
+            const int64_t ko0 = r % p.ko_size[0];
+            const int64_t ko1 = r / p.ko_size[0];
+            const int a2 = src_coord(p.a_src[2], ko0, ko1, c), a3 = src_coord(p.a_src[3], ko0, ko1, c),
+                      a4 = src_coord(p.a_src[4], ko0, ko1, c);
+            const int b2 = src_coord(p.b_src[2], ko0, ko1, c), b3 = src_coord(p.b_src[3], ko0, ko1, c),
+                      b4 = src_coord(p.b_src[4], ko0, ko1, c);
+            uint8_t *dA = sA + stage * Cfg::kABytes + sub * Cfg::kASub;
+            uint8_t *dB = sB + stage * Cfg::kBBytes + sub * Cfg::kBSub;
+            const int kcol = kp * BK;
+            if (!A_MN) {
+              tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
-              tma_load_5d(dA + j * BK * 128, &map_a, &full[stage], mrow + j * Cfg::kRowsPerBox,
-                          kcol, a2, a3, a4);
-          }
-          if (!B_MN) {
-            tma_load_5d(dB, &map_b, &full[stage], kcol, nrow, b2, b3, b4);
-          } else {
+              for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
+                tma_load_5d(dA + j * BK * 128, &map_a, &full[stage], mrow + j * Cfg::kRowsPerBox,
+                            kcol, a2, a3, a4);
+            }
+            if (!B_MN) {
+              tma_load_5d(dB, &map_b, &full[stage], kcol, nrow, b2, b3, b4);
+            } else {
 #pragma unroll
-            for (int j = 0; j < BN / Cfg::kRowsPerBox; ++j)
-              tma_load_5d(dB + j * BK * 128, &map_b, &full[stage], nrow + j * Cfg::kRowsPerBox,
-                          kcol, b2, b3, b4);
+              for (int j = 0; j < BN / Cfg::kRowsPerBox; ++j)
+                tma_load_5d(dB + j * BK * 128, &map_b, &full[stage], nrow + j * Cfg::kRowsPerBox,
+                            kcol, b2, b3, b4);
+            }
           }
           if (++stage == S) {
             stage = 0;
@@ -215,6 +249,13 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
     // ------------------------------------------------------------ MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc = make_idesc(KIND, BM, BN, A_MN, B_MN);
+      // MN-major 32-bit operands use the 32-byte-atom swizzle (4-row K groups)
+      constexpr bool kA32 = A_MN && Cfg::kEsize == 4, kB32 = B_MN && Cfg::kEsize == 4;
+      constexpr uint32_t a_lay = kA32 ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t b_lay = kB32 ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t a_sbo = kA32 ? 512 : 1024, b_sbo = kB32 ? 512 : 1024;
+      constexpr uint32_t a_lbo = A_MN ? BK * 128 : 16;
+      constexpr uint32_t b_lbo = B_MN ? BK * 128 : 16;
       int stage = 0;
       uint32_t phase = 0;
       int acc = 0;
@@ -227,41 +268,43 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        for (int ks = 0; ks < p.k_steps; ++ks) {
+        const int rot = k_rotation(t, n_kstages);
+        for (int js = 0; js < n_kstages; ++js) {
+          int ksg = js + rot;
+          if (ksg >= n_kstages) ksg -= n_kstages;
+          const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
           uint64_t *ready = Cfg::kSplit ? &conv[stage] : &full[stage];
           if (!mbar_wait_bounded(ready, phase, abort_flag)) {
             ok = false;
             break;
           }
           tc_fence_after();
-          const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes);
-          const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes);
 #pragma unroll
-          for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
-            const uint32_t a_off = A_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
-            const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
-            // MN-major 32-bit operands use the 32-byte-atom swizzle (4-row K groups)
-            constexpr bool kA32 = A_MN && Cfg::kEsize == 4, kB32 = B_MN && Cfg::kEsize == 4;
-            constexpr uint32_t a_lay = kA32 ? kLayoutSw128Base32 : kLayoutSw128;
-            constexpr uint32_t b_lay = kB32 ? kLayoutSw128Base32 : kLayoutSw128;
-            constexpr uint32_t a_sbo = kA32 ? 512 : 1024, b_sbo = kB32 ? 512 : 1024;
-            const uint32_t a_lbo = A_MN ? BK * 128 : 16;
-            const uint32_t b_lbo = B_MN ? BK * 128 : 16;
-            const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
-            const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
-            const uint32_t accum = (ks > 0 || kk > 0) ? 1u : 0u;
-            if (KIND == kKindBF16) {
-              umma_f16(d_tmem, adesc, bdesc, idesc, accum);
-            } else if (KIND == kKindTF32) {
-              umma_tf32(d_tmem, adesc, bdesc, idesc, accum);
-            } else {
-              const uint32_t alo_base = smem_u32(sAlo + stage * Cfg::kABytes);
-              const uint32_t blo_base = smem_u32(sBlo + stage * Cfg::kBBytes);
-              const uint64_t alo = make_smem_desc(alo_base + a_off, a_lbo, a_sbo, a_lay);
-              const uint64_t blo = make_smem_desc(blo_base + b_off, b_lbo, b_sbo, b_lay);
-              umma_tf32(d_tmem, alo, bdesc, idesc, accum);  // small terms first
-              umma_tf32(d_tmem, adesc, blo, idesc, 1u);
-              umma_tf32(d_tmem, adesc, bdesc, idesc, 1u);
+          for (int sub = 0; sub < KSUB; ++sub) {
+            if (sub < nsub) {
+              const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes + sub * Cfg::kASub);
+              const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes + sub * Cfg::kBSub);
+#pragma unroll
+              for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+                const uint32_t a_off = A_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+                const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+                const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
+                const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
+                const uint32_t accum = (js > 0 || sub > 0 || kk > 0) ? 1u : 0u;
+                if (KIND == kKindBF16) {
+                  umma_f16(d_tmem, adesc, bdesc, idesc, accum);
+                } else if (KIND == kKindTF32) {
+                  umma_tf32(d_tmem, adesc, bdesc, idesc, accum);
+                } else {
+                  const uint32_t alo_base = smem_u32(sAlo + stage * Cfg::kABytes + sub * Cfg::kASub);
+                  const uint32_t blo_base = smem_u32(sBlo + stage * Cfg::kBBytes + sub * Cfg::kBSub);
+                  const uint64_t alo = make_smem_desc(alo_base + a_off, a_lbo, a_sbo, a_lay);
+                  const uint64_t blo = make_smem_desc(blo_base + b_off, b_lbo, b_sbo, b_lay);
+                  umma_tf32(d_tmem, alo, bdesc, idesc, accum);  // small terms first
+                  umma_tf32(d_tmem, adesc, blo, idesc, 1u);
+                  umma_tf32(d_tmem, adesc, bdesc, idesc, 1u);
+                }
+              }
             }
           }
           umma_commit(&empty[stage]);
@@ -288,7 +331,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
     uint32_t acc_phase = 0;
     for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
       TileCoord c = decode_tile(p, t);
-      if (!mbar_wait_bounded(&tfull[acc], acc_phase, abort_flag)) {
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
         if (!*abort_flag) record_error(p.err, kErrTimeoutEpilogue);
         *abort_flag = 1;
         break;
@@ -303,26 +346,49 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
         ab += c.l[i] * p.loop_sa[i];
       }
       const int64_t n0 = c.nt * BN;
+      const int64_t so_n = p.so_n, sa_n = p.sa_n;
+      // touch kinds with a branch-free column loop: 0 = ZERO first touch and no last
+      // touch, 1 = COPY (bias) first touch with no last touch or RELU; else general
+      const int fast = (p.first_touch == 0 && p.last_touch == 99) ? 0
+                     : (p.first_touch == 3 && (p.last_touch == 99 || p.last_touch == 1)) ? 1 : 2;
+      const bool relu = p.last_touch == 1;
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         uint32_t v[32];
         tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
         tmem_ld_wait();
-        if (mval) {
+        if (!mval) continue;
+        const int64_t nb = n0 + ch * 32;
+        float *op = out + ob + nb * so_n;
+        const float *ap = aux + ab + nb * sa_n;
+        if (fast == 0 && nb + 32 <= p.n_size) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
-            const int64_t n = n0 + ch * 32 + j;
-            if (n < p.n_size) {
+            *op = __uint_as_float(v[j]);
+            op += so_n;
+          }
+        } else if (fast == 1 && nb + 32 <= p.n_size) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]) + __ldg(ap);
+            *op = relu ? fmaxf(x, 0.0f) : x;
+            op += so_n;
+            ap += sa_n;
+          }
+        } else {
+#pragma unroll 4
+          for (int j = 0; j < 32; ++j) {
+            if (nb + j < p.n_size) {
               float x = __uint_as_float(v[j]);
-              const int64_t o = ob + n * p.so_n;
-              const int64_t a = ab + n * p.sa_n;
-              if (p.first_touch == 3 /*COPY*/) x += aux[a];
-              else if (p.first_touch == 2 /*ADD*/) x += out[o] + aux[a];
-              else if (p.first_touch != 0 /*not ZERO*/) x += out[o];
+              if (p.first_touch == 3 /*COPY*/) x += *ap;
+              else if (p.first_touch == 2 /*ADD*/) x += *op + *ap;
+              else if (p.first_touch != 0 /*not ZERO*/) x += *op;
               if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
-              else if (p.last_touch == 2 /*ADD*/) x += aux[a];
-              out[o] = x;
+              else if (p.last_touch == 2 /*ADD*/) x += *ap;
+              *op = x;
             }
+            op += so_n;
+            ap += sa_n;
           }
         }
       }
@@ -339,7 +405,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-      for (int ks = 0; ks < p.k_steps; ++ks) {
+      for (int js = 0; js < n_kstages; ++js) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
           ok = false;
           break;
@@ -347,29 +413,11 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
         float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
         float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kABytes / 16; i += 128) {
-          float4 x = a[i];
-          float4 h, l;
-          h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
-          h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
-          h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
-          h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
-          a[i] = h;
-          alo[i] = l;
-        }
+        for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32(&a[i], &alo[i]);
         float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
         float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) {
-          float4 x = b[i];
-          float4 h, l;
-          h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
-          h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
-          h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
-          h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
-          b[i] = h;
-          blo[i] = l;
-        }
+        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32(&b[i], &blo[i]);
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
         if (++stage == S) {
@@ -393,11 +441,11 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN>::kThreads, 1)
 }
 
 // ---------------------------------------------------------------- launchers
-template <int KIND, int BN, bool A_MN, bool B_MN>
+template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
 static cudaError_t launch_tc_t(CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
                                float const *aux, float *out, int num_sms, cudaStream_t st) {
-  using Cfg = TcConfig<KIND, BN>;
-  auto kern = tc_contract_kernel<KIND, BN, A_MN, B_MN>;
+  using Cfg = TcConfig<KIND, BN, KSUB>;
+  auto kern = tc_contract_kernel<KIND, BN, KSUB, A_MN, B_MN>;
   static unsigned attr_set_mask = 0;  // one bit per device (attribute is per device)
   int dev = 0;
   cudaGetDevice(&dev);
@@ -413,29 +461,37 @@ static cudaError_t launch_tc_t(CUtensorMap const &ma, CUtensorMap const &mb, TcP
   return cudaGetLastError();
 }
 
-template <int KIND, int BN>
+template <int KIND, int BN, int KSUB>
 static cudaError_t launch_tc_major(bool a_mn, bool b_mn, CUtensorMap const &ma,
                                    CUtensorMap const &mb, TcParams const &p, float const *aux,
                                    float *out, int num_sms, cudaStream_t st) {
-  if (!a_mn && !b_mn) return launch_tc_t<KIND, BN, false, false>(ma, mb, p, aux, out, num_sms, st);
-  if (!a_mn && b_mn) return launch_tc_t<KIND, BN, false, true>(ma, mb, p, aux, out, num_sms, st);
-  if (a_mn && !b_mn) return launch_tc_t<KIND, BN, true, false>(ma, mb, p, aux, out, num_sms, st);
-  return launch_tc_t<KIND, BN, true, true>(ma, mb, p, aux, out, num_sms, st);
+  if (!a_mn && !b_mn) return launch_tc_t<KIND, BN, KSUB, false, false>(ma, mb, p, aux, out, num_sms, st);
+  if (!a_mn && b_mn) return launch_tc_t<KIND, BN, KSUB, false, true>(ma, mb, p, aux, out, num_sms, st);
+  if (a_mn && !b_mn) return launch_tc_t<KIND, BN, KSUB, true, false>(ma, mb, p, aux, out, num_sms, st);
+  return launch_tc_t<KIND, BN, KSUB, true, true>(ma, mb, p, aux, out, num_sms, st);
 }
 
-cudaError_t launch_tc_contract(int kind, int bn, bool a_mn, bool b_mn, CUtensorMap const &ma,
-                               CUtensorMap const &mb, TcParams const &p, float const *aux,
-                               float *out, int num_sms, cudaStream_t st) {
-  if (kind == kKindBF16 && bn == 256)
-    return launch_tc_major<kKindBF16, 256>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
-  if (kind == kKindBF16 && bn == 128)
-    return launch_tc_major<kKindBF16, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
-  if (kind == kKindTF32 && bn == 256)
-    return launch_tc_major<kKindTF32, 256>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
-  if (kind == kKindTF32 && bn == 128)
-    return launch_tc_major<kKindTF32, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
-  if (kind == kKind3xTF32 && bn == 128)
-    return launch_tc_major<kKind3xTF32, 128>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
+                               CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
+                               float const *aux, float *out, int num_sms, cudaStream_t st) {
+  if (kind == kKindBF16 && bn == 256 && ksub == 1)
+    return launch_tc_major<kKindBF16, 256, 1>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindBF16 && bn == 256 && ksub == 2)
+    return launch_tc_major<kKindBF16, 256, 2>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindBF16 && bn == 128 && ksub == 1)
+    return launch_tc_major<kKindBF16, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindBF16 && bn == 128 && ksub == 2)
+    return launch_tc_major<kKindBF16, 128, 2>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 256 && ksub == 1)
+    return launch_tc_major<kKindTF32, 256, 1>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 256 && ksub == 2)
+    return launch_tc_major<kKindTF32, 256, 2>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 128 && ksub == 1)
+    return launch_tc_major<kKindTF32, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKindTF32 && bn == 128 && ksub == 2)
+    return launch_tc_major<kKindTF32, 128, 2>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
+  if (kind == kKind3xTF32 && bn == 128 && ksub == 1)
+    return launch_tc_major<kKind3xTF32, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, num_sms, st);
   return cudaErrorInvalidValue;
 }
 
