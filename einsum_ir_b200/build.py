@@ -23,7 +23,7 @@ ROOT = PKG.parent
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 COMMON = ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-Xcompiler", "-Wall",
-          f"-I{ROOT / 'include'}", f"-I{CSRC}"]
+          f"-I{ROOT / 'include'}", f"-I{CSRC}", f"-I{CSRC / 'host'}"]
 
 
 def _nvcc() -> str:
@@ -75,7 +75,10 @@ def build(verbose: bool = False, jobs: int | None = None) -> Path:
 
 
 def _build_drivers(verbose: bool) -> None:
-    drivers = sorted((CSRC / "drivers").glob("*.cpp")) if (CSRC / "drivers").exists() else []
+    drivers = []
+    for sub in ("drivers", "tests"):
+        if (CSRC / sub).exists():
+            drivers += sorted((CSRC / sub).glob("*.cpp"))
     for src in drivers:
         exe = PKG / src.stem
         if exe.exists() and exe.stat().st_mtime >= max(src.stat().st_mtime, LIB.stat().st_mtime):

@@ -449,6 +449,17 @@ bool try_tc(eir_plan *p, std::string *why) {
     int64_t force = env_int("EIR_TC_BN", 0);  // tuning override: 128 or 256
     if (force == 128 || force == 256) bn = (int)force;
   }
+  // a 128 x BN tile over tiny primitive M / N dims wastes most of each MMA
+  {
+    double um = (double)d[mp].size / (double)(ceil_div(d[mp].size, 128) * 128);
+    double un = (double)d[np].size / (double)(ceil_div(d[np].size, bn) * bn);
+    char const *v = std::getenv("EIR_TC_MIN_UTIL");
+    double min_util = (v != nullptr && *v) ? std::atof(v) : 0.25;
+    if (um * un < min_util) {
+      *why = "tile utilisation of the primitive M/N dims below threshold";
+      return false;
+    }
+  }
 
   // TMA maps
   auto fill_map = [&](eir::MapSpec &ms, bool left, bool mn, int rowdim, int rows) -> bool {

@@ -46,6 +46,7 @@ def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
              tf32_general=False, tc_min_ops="0"):
     import torch
     os.environ["EIR_TC_MIN_OPS"] = tc_min_ops
+    os.environ["EIR_TC_MIN_UTIL"] = "0"
     il, ir, io, names = binary.parse_binary(expr)
     sz = {i: sizes[c] for i, c in enumerate(names)}
     aux_sizes = None
