@@ -283,11 +283,13 @@ bool try_tc(eir_plan *p, std::string *why) {
     kind = 0;
   } else if (p->dt_l == EIR_FP32 && p->dt_r == EIR_FP32 && p->dt_o == EIR_FP32) {
     kind = (p->comp == EIR_COMPUTE_TF32) ? 1 : 2;
+  } else if (p->dt_l == EIR_FP64 && p->dt_r == EIR_FP64 && p->dt_o == EIR_FP64) {
+    kind = 3;  // FP64 tensor cores (DMMA)
   } else {
     *why = "dtype has no tensor-core path";
     return false;
   }
-  const int esize = kind == 0 ? 2 : 4;
+  const int esize = kind == 0 ? 2 : (kind == 3 ? 8 : 4);
   int nc = 0, nm = 0, nn = 0, nk = 0;
   for (auto const &x : d) {
     if (x.size <= 0 || x.size >= (int64_t(1) << 31)) {
@@ -441,7 +443,7 @@ bool try_tc(eir_plan *p, std::string *why) {
   int num_sms = 148;
   if (device_state(&ds) == EIR_SUCCESS) num_sms = ds->num_sms;
   int bn = 128;
-  if (kind != 2) {
+  if (kind != 2 && kind != 3) {
     int64_t t128 = tiles_base * ceil_div(d[np].size, 128), t256 = tiles_base * ceil_div(d[np].size, 256);
     double c128 = (double)ceil_div(t128, num_sms) * (128 + 32);
     double c256 = (double)ceil_div(t256, num_sms) * (256 + 32);
@@ -463,7 +465,8 @@ bool try_tc(eir_plan *p, std::string *why) {
 
   // TMA maps
   auto fill_map = [&](eir::MapSpec &ms, bool left, bool mn, int rowdim, int rows) -> bool {
-    ms.dtype = (kind == 0) ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
+    ms.dtype = kind == 0 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+             : kind == 3 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT64 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32;
     // 32-bit MN-major operands: the only tcgen05 layout is 128B swizzle with 32B atoms
     ms.swizzle = (mn && esize == 4) ? CU_TENSOR_MAP_SWIZZLE_128B_ATOM_32B : CU_TENSOR_MAP_SWIZZLE_128B;
     auto st = [&](int i) { return left ? sl_of(i) : sr_of(i); };
@@ -549,9 +552,10 @@ bool try_tc(eir_plan *p, std::string *why) {
   t.last_touch = p->last;
   t.group_m = (int32_t)std::max<int64_t>(1, env_int("EIR_TC_GROUP_M", 16));
   // K blocks per ring stage: two (larger stages) whenever there are at least two K blocks
-  int ksub = (kind != 2 && t.k_steps >= 2) ? 2 : 1;
+  const bool ksub_ok = kind == 0 || kind == 1;  // 3xTF32 and FP64 use one K block per stage
+  int ksub = (ksub_ok && t.k_steps >= 2) ? 2 : 1;
   int64_t force_ksub = env_int("EIR_TC_KSUB", 0);  // tuning override: 1 or 2
-  if (kind != 2 && (force_ksub == 1 || force_ksub == 2)) ksub = (int)force_ksub;
+  if (ksub_ok && (force_ksub == 1 || force_ksub == 2)) ksub = (int)force_ksub;
   p->tc_ksub = ksub;
 
   p->tc = true;
@@ -588,7 +592,8 @@ bool try_tc(eir_plan *p, std::string *why) {
   std::snprintf(buf, sizeof(buf),
                 "tc kind=%s BN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
                 "tiles=%lld ksteps=%d prepack=%s",
-                kind == 0 ? "bf16" : (kind == 1 ? "tf32" : "3xtf32"), bn, p->tc_ksub, a_mn ? "MN" : "K",
+                kind == 0 ? "bf16" : kind == 1 ? "tf32" : kind == 2 ? "3xtf32" : "fp64-dmma", bn,
+                p->tc_ksub, a_mn ? "MN" : "K",
                 b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
                 (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
                 (long long)t.total_tiles, t.k_steps,
@@ -729,7 +734,7 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
 
   std::string why = "forced";
   if (!p->empty && !(desc->flags & EIR_FLAG_FORCE_SIMT) && try_tc(p, &why)) {
-    p->family = EIR_FAMILY_TC;
+    p->family = p->tc_kind == 3 ? EIR_FAMILY_DMMA : EIR_FAMILY_TC;
   } else {
     p->family = EIR_FAMILY_SIMT;
   }
@@ -738,7 +743,8 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
     dims_txt += type_name(x.type);
     dims_txt += std::to_string(x.size) + " ";
   }
-  p->text = (p->family == EIR_FAMILY_TC ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
+  const bool tensor_cores = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
+  p->text = (tensor_cores ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
   *plan_out = p;
   return EIR_SUCCESS;
 }
@@ -751,7 +757,7 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   bool uses_aux = p->first == EIR_KTYPE_COPY || p->first == EIR_KTYPE_ADD || p->last == EIR_KTYPE_ADD;
   if (uses_aux && aux == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
-  if (p->family != EIR_FAMILY_TC) return run_simt(p, l, r, aux, out, st);
+  if (p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA) return run_simt(p, l, r, aux, out, st);
 
   DeviceState *ds = nullptr;
   int rc = device_state(&ds);
@@ -804,9 +810,13 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
   ProfScope prof(p, st);
-  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
-                                          static_cast<float const *>(aux), static_cast<float *>(out),
-                                          ds->num_sms, st);
+  cudaError_t e =
+      p->tc_kind == 3
+          ? eir::launch_dmma_contract(p->a_mn, p->b_mn, ma, mb, tp, static_cast<double const *>(aux),
+                                      static_cast<double *>(out), ds->num_sms, st)
+          : eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
+                                    static_cast<float const *>(aux), static_cast<float *>(out),
+                                    ds->num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;

@@ -19,6 +19,12 @@ cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
                                CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
                                float const *aux, float *out, int num_sms, cudaStream_t st);
 
+// FP64 on the FP64 tensor cores (mma.sync m8n8k4), 128 x 128 tiles, K blocks of 16
+cudaError_t launch_dmma_contract(bool a_mn, bool b_mn, CUtensorMap const &ma, CUtensorMap const &mb,
+                                 TcParams const &p, double const *aux, double *out, int num_sms,
+                                 cudaStream_t st);
+
+// K elements per block (one 128-byte swizzle row): 64 BF16, 32 FP32/TF32, 16 FP64
 int tc_block_k(int kind);
 
 }  // namespace eir

@@ -102,7 +102,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   cudaStream_t st = static_cast<cudaStream_t>(stream);
 
   const bool aligned = !((reinterpret_cast<uintptr_t>(l) | reinterpret_cast<uintptr_t>(r)) & 15);
-  if (p->family != EIR_FAMILY_TC || !aligned) {
+  if ((p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA) || !aligned) {
     cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt, l, r, aux, out, st);
     if (e != cudaSuccess) return eir::api_cuda_fail(e, "simt contraction launch");
     eir::api_count_launch();
@@ -148,9 +148,13 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   }
   eir::TcParams tp = p->tcp;
   tp.err = reinterpret_cast<uint32_t *>(d->scratch);  // header word
-  cudaError_t e = eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
-                                          static_cast<float const *>(aux), static_cast<float *>(out),
-                                          d->num_sms, st);
+  cudaError_t e =
+      p->tc_kind == 3
+          ? eir::launch_dmma_contract(p->a_mn, p->b_mn, ma, mb, tp, static_cast<double const *>(aux),
+                                      static_cast<double *>(out), d->num_sms, st)
+          : eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
+                                    static_cast<float const *>(aux), static_cast<float *>(out),
+                                    d->num_sms, st);
   if (e != cudaSuccess) return eir::api_cuda_fail(e, "tc contraction launch");
   eir::api_count_launch();
   return EIR_SUCCESS;

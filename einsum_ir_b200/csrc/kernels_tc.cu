@@ -495,6 +495,6 @@ cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
   return cudaErrorInvalidValue;
 }
 
-int tc_block_k(int kind) { return kind == kKindBF16 ? 64 : 32; }
+int tc_block_k(int kind) { return kind == kKindBF16 ? 64 : (kind == 3 ? 16 : 32); }
 
 }  // namespace eir

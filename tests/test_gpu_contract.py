@@ -142,6 +142,29 @@ def test_tc_touch_kernels(cuda, first, last):
              aux_outer="n", expect_family=TC)
 
 
+DMMA = cabi.FAMILY_DMMA
+
+DMMA_CASES = [
+    ("mk,nk->nm", dict(m=256, n=384, k=64), "fp64"),        # A K-major, B K-major
+    ("km,nk->nm", dict(m=256, n=384, k=48), "fp64"),        # A MN-major, B K-major
+    ("mk,kn->nm", dict(m=256, n=384, k=48), "fp64"),        # A K-major, B MN-major
+    ("km,kn->nm", dict(m=256, n=384, k=80), "fp64"),        # both MN-major
+    ("mk,nk->nm", dict(m=130, n=70, k=34), "fp64"),         # ragged tails
+    ("zcdef,zabcd->zabef", dict(z=3, a=8, b=8, c=8, d=8, e=8, f=8), "fp64"),
+    ("axmk,nkx->anm", dict(a=3, x=2, m=96, k=64, n=80), "fp64"),
+]
+
+
+@pytest.mark.parametrize("expr,sizes,dtype", DMMA_CASES)
+def test_dmma_parity(cuda, expr, sizes, dtype):
+    run_case(cuda, expr, sizes, dtype, expect_family=DMMA)
+
+
+def test_dmma_bias_relu(cuda):
+    run_case(cuda, "io,bi->bo", dict(b=256, i=96, o=192), "fp64", first=cabi.KTYPE_COPY,
+             last=cabi.KTYPE_RELU, aux_outer="b", expect_family=DMMA)
+
+
 SIMT_CASES = [
     ("bf,dcba->acdf", dict(a=4, b=3, c=5, d=8, f=2), "fp32"),
     ("dh,acdf->acfh", dict(a=4, c=5, d=8, f=2, h=9), "fp32"),
