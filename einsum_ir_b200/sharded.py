@@ -1,0 +1,178 @@
+"""Batch-sharded binary contraction across the GPUs of one node.
+
+The output's outermost dim (a C or M dim, e.g. z in BASELINE config 5
+``zabcd,zcdef->zabef``) is split into ``world * chunks`` blocks. Rank r owns
+blocks ``c * world + r`` (c = 0..chunks-1), so block c of all ranks together is
+one contiguous slice of the output: after computing its block c a rank
+all-gathers it straight into that slice (``all_gather_into_tensor``, NCCL over
+NVLink), on a communication stream, while it computes block c+1. The
+contraction itself is the C-ABI plan of one block (one process per GPU;
+torch.distributed is only the plumbing).
+
+``python -m einsum_ir_b200.sharded`` (under torchrun) runs config 5 and prints
+one JSON line per rank 0.
+"""
+from __future__ import annotations
+
+import json
+import os
+import sys
+from dataclasses import dataclass
+from typing import Callable, List, Sequence
+
+from . import binary, cabi
+
+
+@dataclass
+class ShardLayout:
+    """Which blocks of the sharded dim a rank owns and where they land."""
+    size: int      # extent of the sharded dim
+    world: int
+    chunks: int
+
+    @property
+    def block(self) -> int:
+        if self.size % (self.world * self.chunks):
+            raise ValueError("sharded dim must divide into world * chunks blocks")
+        return self.size // (self.world * self.chunks)
+
+    def owned(self, rank: int) -> List[int]:
+        """Start index (in the sharded dim) of each block rank `rank` computes, in order."""
+        return [(c * self.world + rank) * self.block for c in range(self.chunks)]
+
+    def gathered_range(self, c: int) -> range:
+        """Indices of the sharded dim filled by the all-gather of block round c."""
+        b = self.block
+        return range(c * self.world * b, (c + 1) * self.world * b)
+
+
+def run_sharded(layout: ShardLayout, rank: int, compute: Callable[[int, int], object],
+                out_rows: Callable[[range], object], gather: Callable[[object, object], None],
+                wait: Callable[[], None] | None = None) -> None:
+    """Drives the block rounds: compute(c, start) returns the local block
+    result, out_rows(range) the destination slice, gather(dst, src) enqueues the
+    all-gather (which may overlap the next compute); wait() drains it."""
+    for c, start in enumerate(layout.owned(rank)):
+        local = compute(c, start)
+        gather(out_rows(layout.gathered_range(c)), local)
+    if wait is not None:
+        wait()
+
+
+class ShardedContraction:
+    """Config-5 style contraction with the sharded dim outermost in every tensor."""
+
+    def __init__(self, expr: str, sizes: dict, dtype: int, world: int, rank: int, chunks: int = 4,
+                 dtype_comp: int = cabi.COMPUTE_DEFAULT):
+        il, ir, io, names = binary.parse_binary(expr)
+        self.shard_dim = io[0]
+        for ids in (il, ir):
+            if self.shard_dim in ids and ids[0] != self.shard_dim:
+                raise ValueError("the sharded dim must be outermost in every tensor holding it")
+        self.names, self.il, self.ir, self.io = names, il, ir, io
+        self.sizes = {i: sizes[c] for i, c in enumerate(names)}
+        self.layout = ShardLayout(self.sizes[self.shard_dim], world, chunks)
+        blk = dict(self.sizes)
+        blk[self.shard_dim] = self.layout.block
+        self.block_sizes = blk
+        dto = cabi.FP64 if dtype == cabi.FP64 else cabi.FP32
+        self.plan = cabi.ContractPlan(binary.contraction_dims(il, ir, io, blk), dtype, dtype, dto,
+                                      dtype_comp)
+        self.world, self.rank = world, rank
+        self.num_ops = self.plan.num_ops * world * chunks
+
+    def shape(self, ids: Sequence[int], block: bool = False):
+        s = self.block_sizes if block else self.sizes
+        return [s[i] for i in ids]
+
+    def run(self, left, right, out, comm_stream=None):
+        """left/right: this rank's full-size inputs (only its blocks are read);
+        out: full output on every rank (filled by the all-gathers)."""
+        import torch
+        import torch.distributed as dist
+        lay = self.layout
+        compute_stream = torch.cuda.current_stream()
+        comm = comm_stream or torch.cuda.Stream()
+        locals_ = []
+
+        def compute(c, start):
+            blk = torch.empty(self.shape(self.io, True), dtype=out.dtype, device=out.device)
+            lsl = left[start:start + lay.block] if self.shard_dim in self.il else left
+            rsl = right[start:start + lay.block] if self.shard_dim in self.ir else right
+            self.plan.contract(lsl, rsl, blk, stream=compute_stream.cuda_stream)
+            ev = torch.cuda.Event()
+            ev.record(compute_stream)
+            locals_.append((blk, ev))
+            return len(locals_) - 1
+
+        def gather(dst, idx):
+            blk, ev = locals_[idx]
+            comm.wait_event(ev)
+            blk.record_stream(comm)  # the caching allocator must not reuse it before the gather ends
+            with torch.cuda.stream(comm):
+                if self.world > 1:
+                    dist.all_gather_into_tensor(dst, blk)
+                else:
+                    dst.copy_(blk)
+
+        run_sharded(lay, self.rank, compute, lambda rg: out[rg.start:rg.stop], gather,
+                    lambda: compute_stream.wait_stream(comm))
+
+
+def _main() -> int:
+    import time
+    import torch
+    import torch.distributed as dist
+    from datetime import timedelta
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    dt = cabi.FP64 if "--fp32" not in sys.argv else cabi.FP32
+    comp = cabi.COMPUTE_TF32 if "--tf32" in sys.argv else cabi.COMPUTE_DEFAULT
+    sizes = dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48)
+    sc = ShardedContraction("zabcd,zcdef->zabef", sizes, dt, world, rank, chunks=4 if world < 8 else 2,
+                            dtype_comp=comp)
+    tdt = torch.float64 if dt == cabi.FP64 else torch.float32
+    g = torch.Generator(device=dev).manual_seed(7)
+    left = torch.rand(sc.shape(sc.il), generator=g, device=dev, dtype=tdt)
+    right = torch.rand(sc.shape(sc.ir), generator=g, device=dev, dtype=tdt)
+    out = torch.empty(sc.shape(sc.io), device=dev, dtype=tdt)
+    for _ in range(2):
+        sc.run(left, right, out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    steps = 3
+    e0.record()
+    for _ in range(steps):
+        sc.run(left, right, out)
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / steps
+    t = torch.tensor([ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    # spot check one gathered block of another rank against torch
+    zz = sc.layout.owned((rank + 1) % world)[0]
+    ref = torch.einsum("abcd,cdef->abef", left[zz], right[zz])
+    rel = float((out[zz] - ref).norm() / ref.norm())
+    if rank == 0:
+        print(json.dumps({"config": "zabcd,zcdef->zabef z=64 a..f=48", "dtype": "fp64" if dt == cabi.FP64 else
+                          ("tf32" if comp == cabi.COMPUTE_TF32 else "fp32"), "gpus": world,
+                          "ms_per_eval_max_over_ranks": float(t.item()),
+                          "tflops": sc.num_ops / (float(t.item()) * 1e-3) / 1e12,
+                          "timed": "compute + all-gather of the full output", "rel_err_check": rel}),
+              flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(_main())

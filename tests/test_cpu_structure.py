@@ -135,7 +135,8 @@ PLAN_CASES = [
      cabi.COMPUTE_TF32, ["tc kind=tf32", "A=MN B=K", "M=2304 N=2304 Kp=2304"]),
     ("io,bi->bo", dict(b=8192, i=4096, o=4096), cabi.FP32, 0, ["tc kind=3xtf32", "A=MN B=K"]),
     ("io,bi->bo", dict(b=8192, i=4096, o=4096), cabi.BF16, 0, ["tc kind=bf16", "A=MN B=K"]),
-    ("zcdef,zabcd->zabef", dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48), cabi.FP64, 0, ["simt"]),
+    ("zcdef,zabcd->zabef", dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48), cabi.FP64, 0,
+     ["tc kind=fp64-dmma", "A=MN B=K"]),
     ("acfh,acegi->hgfei", dict(a=32, c=4, e=16, f=64, g=8, h=8, i=8), cabi.FP32, 0, ["simt"]),
 ]
 
