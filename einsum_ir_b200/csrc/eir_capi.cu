@@ -436,24 +436,45 @@ bool try_tc(eir_plan *p, std::string *why) {
   }
 
   const int bk = eir::tc_block_k(kind);
-  // BN: minimise waves x (BN + fixed per-tile overhead)
-  int64_t tiles_base = ceil_div(d[mp].size, 128);
-  for (int i : loops) tiles_base *= d[i].size;
+  // Tile shape. One CTA per 128 x BN tile stages 128 + BN operand rows per K
+  // block; a CTA pair (256 x BN over two SMs, kinds BF16 / TF32) stages
+  // 128 + BN/2 rows per SM for the same 128 x BN outputs per SM. Operand rows
+  // staged per SM (the L2 -> SM traffic) set the time of a tile once K is
+  // long; minimise waves x (rows per SM + a fixed per-tile overhead).
+  int64_t loop_tiles = 1;
+  for (int i : loops) loop_tiles *= d[i].size;
   DeviceState *ds = nullptr;
   int num_sms = 148;
   if (device_state(&ds) == EIR_SUCCESS) num_sms = ds->num_sms;
   int bn = 128;
+  bool pair = false;
   if (kind != 2 && kind != 3) {
-    int64_t t128 = tiles_base * ceil_div(d[np].size, 128), t256 = tiles_base * ceil_div(d[np].size, 256);
-    double c128 = (double)ceil_div(t128, num_sms) * (128 + 32);
-    double c256 = (double)ceil_div(t256, num_sms) * (256 + 32);
-    bn = (d[np].size > 128 && c256 <= c128) ? 256 : 128;
-    int64_t force = env_int("EIR_TC_BN", 0);  // tuning override: 128 or 256
-    if (force == 128 || force == 256) bn = (int)force;
+    const int64_t force_bn = env_int("EIR_TC_BN", 0);     // tuning override: 128 or 256
+    const int64_t force_pair = env_int("EIR_TC_PAIR", -1);  // tuning override: 0 or 1
+    double best = 0.0;
+    for (int pr = 0; pr < 2; ++pr) {
+      if (force_pair == 0 && pr == 1) continue;
+      if (force_pair == 1 && pr == 0 && d[mp].size > 128) continue;
+      if (pr == 1 && d[mp].size <= 128) continue;  // a pair tile would be half empty
+      for (int cbn : {128, 256}) {
+        if ((force_bn == 128 || force_bn == 256) && cbn != force_bn) continue;
+        if (cbn == 256 && d[np].size <= 128 && force_bn != 256) continue;
+        const int64_t tiles = ceil_div(d[mp].size, pr ? 256 : 128) * ceil_div(d[np].size, cbn) *
+                              loop_tiles;
+        const int64_t slots = pr ? std::max(1, num_sms / 2) : num_sms;
+        const double cost = (double)ceil_div(tiles, slots) * (128 + (pr ? cbn / 2 : cbn) + 64);
+        if (best == 0.0 || cost < best) {
+          best = cost;
+          bn = cbn;
+          pair = pr == 1;
+        }
+      }
+    }
   }
+  const int tile_m = pair ? 256 : 128;
   // a 128 x BN tile over tiny primitive M / N dims wastes most of each MMA
   {
-    double um = (double)d[mp].size / (double)(ceil_div(d[mp].size, 128) * 128);
+    double um = (double)d[mp].size / (double)(ceil_div(d[mp].size, tile_m) * tile_m);
     double un = (double)d[np].size / (double)(ceil_div(d[np].size, bn) * bn);
     char const *v = std::getenv("EIR_TC_MIN_UTIL");
     double min_util = (v != nullptr && *v) ? std::atof(v) : 0.25;
@@ -516,7 +537,7 @@ bool try_tc(eir_plan *p, std::string *why) {
     *why = "left operand strides not TMA-compatible";
     return false;
   }
-  if (!fill_map(p->map_b, false, b_mn, np, bn)) {
+  if (!fill_map(p->map_b, false, b_mn, np, pair ? bn / 2 : bn)) {
     *why = "right operand strides not TMA-compatible";
     return false;
   }
@@ -537,7 +558,7 @@ bool try_tc(eir_plan *p, std::string *why) {
   }
   t.ko_size[0] = ko.size() > 0 ? d[ko[0]].size : 1;
   t.ko_size[1] = ko.size() > 1 ? d[ko[1]].size : 1;
-  t.m_tiles = (int32_t)ceil_div(t.m_size, 128);
+  t.m_tiles = (int32_t)ceil_div(t.m_size, tile_m);
   t.n_tiles = (int32_t)ceil_div(t.n_size, bn);
   t.kp_blocks = (int32_t)ceil_div(t.kp_size, bk);
   int64_t ksteps = (int64_t)t.kp_blocks * t.ko_size[0] * t.ko_size[1];
@@ -561,6 +582,7 @@ bool try_tc(eir_plan *p, std::string *why) {
   p->tc = true;
   p->tc_kind = kind;
   p->tc_bn = bn;
+  p->tc_pair = pair;
   p->a_mn = a_mn;
   p->b_mn = b_mn;
   p->tc_esize = esize;
@@ -590,9 +612,10 @@ bool try_tc(eir_plan *p, std::string *why) {
 
   char buf[512];
   std::snprintf(buf, sizeof(buf),
-                "tc kind=%s BN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
+                "tc kind=%s %sBN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
                 "tiles=%lld ksteps=%d prepack=%s",
-                kind == 0 ? "bf16" : kind == 1 ? "tf32" : kind == 2 ? "3xtf32" : "fp64-dmma", bn,
+                kind == 0 ? "bf16" : kind == 1 ? "tf32" : kind == 2 ? "3xtf32" : "fp64-dmma",
+                pair ? "pair BM=256 " : "", bn,
                 p->tc_ksub, a_mn ? "MN" : "K",
                 b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
                 (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
@@ -652,6 +675,18 @@ int api_set_error(int code, char const *msg) { return set_error(code, msg); }
 int api_cuda_fail(cudaError_t e, char const *where) { return cuda_fail(e, where); }
 int api_encode_map(MapSpec const &s, void const *ptr, CUtensorMap *m) { return encode_map(s, ptr, m); }
 void api_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+cudaError_t api_launch_tc(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
+                          TcParams const &tp, void const *aux, void *out, int num_sms,
+                          cudaStream_t st) {
+  if (p->tc_kind == 3)
+    return launch_dmma_contract(p->a_mn, p->b_mn, ma, mb, tp, static_cast<double const *>(aux),
+                                static_cast<double *>(out), num_sms, st);
+  if (p->tc_pair)
+    return launch_tc_pair_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
+                                   static_cast<float const *>(aux), static_cast<float *>(out), st);
+  return launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
+                            static_cast<float const *>(aux), static_cast<float *>(out), num_sms, st);
+}
 }  // namespace eir
 
 // =================================================================== C-ABI
@@ -810,13 +845,7 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
   ProfScope prof(p, st);
-  cudaError_t e =
-      p->tc_kind == 3
-          ? eir::launch_dmma_contract(p->a_mn, p->b_mn, ma, mb, tp, static_cast<double const *>(aux),
-                                      static_cast<double *>(out), ds->num_sms, st)
-          : eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
-                                    static_cast<float const *>(aux), static_cast<float *>(out),
-                                    ds->num_sms, st);
+  cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, ds->num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;

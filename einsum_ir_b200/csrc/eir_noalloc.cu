@@ -148,13 +148,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   }
   eir::TcParams tp = p->tcp;
   tp.err = reinterpret_cast<uint32_t *>(d->scratch);  // header word
-  cudaError_t e =
-      p->tc_kind == 3
-          ? eir::launch_dmma_contract(p->a_mn, p->b_mn, ma, mb, tp, static_cast<double const *>(aux),
-                                      static_cast<double *>(out), d->num_sms, st)
-          : eir::launch_tc_contract(p->tc_kind, p->tc_bn, p->tc_ksub, p->a_mn, p->b_mn, ma, mb, tp,
-                                    static_cast<float const *>(aux), static_cast<float *>(out),
-                                    d->num_sms, st);
+  cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, d->num_sms, st);
   if (e != cudaSuccess) return eir::api_cuda_fail(e, "tc contraction launch");
   eir::api_count_launch();
   return EIR_SUCCESS;

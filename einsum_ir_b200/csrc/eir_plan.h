@@ -42,6 +42,14 @@ void api_count_launch();
 
 }  // namespace eir
 
+struct eir_plan;
+namespace eir {
+// launches the tensor-core kernel a plan chose (DMMA, CTA-pair tcgen05 or one-CTA tcgen05)
+cudaError_t api_launch_tc(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
+                          TcParams const &tp, void const *aux, void *out, int num_sms,
+                          cudaStream_t st);
+}  // namespace eir
+
 struct eir_plan {
   int what = 0;  // 1 = contraction, 2 = permute
   int family = EIR_FAMILY_NONE;
@@ -56,6 +64,7 @@ struct eir_plan {
   eir::SimtParams simt;
   bool tc = false;
   int tc_kind = 0, tc_bn = 128, tc_ksub = 1;
+  bool tc_pair = false;  // CTA-pair (cta_group::2) kernel, 256-row tiles
   bool a_mn = false, b_mn = false;
   eir::TcParams tcp{};
   eir::MapSpec map_a, map_b;

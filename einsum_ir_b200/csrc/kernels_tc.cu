@@ -29,10 +29,9 @@
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
+#include "tc_tile.cuh"
 
 namespace eir {
-
-enum { kKindBF16 = 0, kKindTF32 = 1, kKind3xTF32 = 2 };
 
 template <int KIND, int BN, int KSUB>
 struct TcConfig {
@@ -56,68 +55,6 @@ struct TcConfig {
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
-
-// instruction descriptor for kind::f16 (bf16) / kind::tf32, FP32 accumulate
-__host__ __device__ constexpr uint32_t make_idesc(int kind, int m, int n, bool a_mn, bool b_mn) {
-  uint32_t fmt = (kind == kKindBF16) ? 1u : 2u;  // BF16 = 1, TF32 = 2
-  return (1u << 4)                               // D format F32
-         | (fmt << 7) | (fmt << 10)              // A / B format
-         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
-         | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
-}
-
-struct TileCoord {
-  int64_t mt, nt;
-  int64_t l[kMaxTileLoops];
-};
-
-// tile index -> (M tile, N tile, tile-loop indices); M/N tiles in groups of group_m M tiles
-__device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
-  TileCoord c;
-  const int64_t mn = (int64_t)p.m_tiles * p.n_tiles;
-  int64_t u = t % mn;
-  t /= mn;
-  const int64_t gsz_full = (int64_t)p.group_m * p.n_tiles;
-  const int64_t g = u / gsz_full;
-  const int64_t first_m = g * p.group_m;
-  const int64_t rem_m = p.m_tiles - first_m;
-  const int64_t gm = rem_m < p.group_m ? rem_m : p.group_m;
-  const int64_t r = u - g * gsz_full;
-  c.mt = first_m + r % gm;
-  c.nt = r / gm;
-#pragma unroll
-  for (int i = 0; i < kMaxTileLoops; ++i) {
-    if (i < p.n_loops) {
-      c.l[i] = t % p.loop_size[i];
-      t /= p.loop_size[i];
-    } else {
-      c.l[i] = 0;
-    }
-  }
-  return c;
-}
-
-__device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, TileCoord const &c) {
-  switch (src) {
-    case kSrcKo0: return (int)ko0;
-    case kSrcKo1: return (int)ko1;
-    case kSrcLoop0: return (int)c.l[0];
-    case kSrcLoop0 + 1: return (int)c.l[1];
-    case kSrcLoop0 + 2: return (int)c.l[2];
-    case kSrcLoop0 + 3: return (int)c.l[3];
-    default: return 0;
-  }
-}
-
-// Start offset (in stages) of a tile's K walk. Tiles running at the same time
-// start at different K positions so they do not all fetch the same operand
-// lines at once (the sum over K is order independent up to FP32 rounding).
-// Producer and MMA issuer only need to agree on the order of stages; the first
-// MMA of a tile's walk always initialises the accumulator.
-__device__ __forceinline__ int k_rotation(int64_t t, int n_stages) {
-  if (n_stages <= 1) return 0;
-  return (int)((t * 7) % n_stages);
-}
 
 __device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
   uint32_t r;
@@ -198,6 +135,9 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         TileCoord c = decode_tile(p, t);
         const int rot = k_rotation(t, n_kstages);
         const int mrow = (int)(c.mt * BM), nrow = (int)(c.nt * BN);
+        const SlotCoords sa = slot_coords(p.a_src, c), sb = slot_coords(p.b_src, c);
+        KWalk kw;
+        kw.seek(p, rot * KSUB);
         for (int js = 0; js < n_kstages; ++js) {
           int ksg = js + rot;
           if (ksg >= n_kstages) ksg -= n_kstages;
@@ -208,19 +148,14 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           }
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
           mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
-          for (int sub = 0; sub < nsub; ++sub) {
-            const int ks = ksg * KSUB + sub;
-            const int kp = ks % p.kp_blocks;
-            const int64_t r = ks / p.kp_blocks;
-            const int64_t ko0 = r % p.ko_size[0];
-            const int64_t ko1 = r / p.ko_size[0];
-            const int a2 = src_coord(p.a_src[2], ko0, ko1, c), a3 = src_coord(p.a_src[3], ko0, ko1, c),
-                      a4 = src_coord(p.a_src[4], ko0, ko1, c);
-            const int b2 = src_coord(p.b_src[2], ko0, ko1, c), b3 = src_coord(p.b_src[3], ko0, ko1, c),
-                      b4 = src_coord(p.b_src[4], ko0, ko1, c);
+          for (int sub = 0; sub < nsub; ++sub, kw.next(p)) {
+            const int a2 = slot_at(sa, 0, kw.ko0, kw.ko1), a3 = slot_at(sa, 1, kw.ko0, kw.ko1),
+                      a4 = slot_at(sa, 2, kw.ko0, kw.ko1);
+            const int b2 = slot_at(sb, 0, kw.ko0, kw.ko1), b3 = slot_at(sb, 1, kw.ko0, kw.ko1),
+                      b4 = slot_at(sb, 2, kw.ko0, kw.ko1);
             uint8_t *dA = sA + stage * Cfg::kABytes + sub * Cfg::kASub;
             uint8_t *dB = sB + stage * Cfg::kBBytes + sub * Cfg::kBSub;
-            const int kcol = kp * BK;
+            const int kcol = kw.kp * BK;
             if (!A_MN) {
               tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
             } else {
@@ -347,11 +282,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
       }
       const int64_t n0 = c.nt * BN;
       const int64_t so_n = p.so_n, sa_n = p.sa_n;
-      // touch kinds with a branch-free column loop: 0 = ZERO first touch and no last
-      // touch, 1 = COPY (bias) first touch with no last touch or RELU; else general
-      const int fast = (p.first_touch == 0 && p.last_touch == 99) ? 0
-                     : (p.first_touch == 3 && (p.last_touch == 99 || p.last_touch == 1)) ? 1 : 2;
-      const bool relu = p.last_touch == 1;
+      const int fast = epilogue_kind(p);
 #pragma unroll 1
       for (int ch = 0; ch < BN / 32; ++ch) {
         uint32_t v[32];
@@ -359,38 +290,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         tmem_ld_wait();
         if (!mval) continue;
         const int64_t nb = n0 + ch * 32;
-        float *op = out + ob + nb * so_n;
-        const float *ap = aux + ab + nb * sa_n;
-        if (fast == 0 && nb + 32 <= p.n_size) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            *op = __uint_as_float(v[j]);
-            op += so_n;
-          }
-        } else if (fast == 1 && nb + 32 <= p.n_size) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(v[j]) + __ldg(ap);
-            *op = relu ? fmaxf(x, 0.0f) : x;
-            op += so_n;
-            ap += sa_n;
-          }
-        } else {
-#pragma unroll 4
-          for (int j = 0; j < 32; ++j) {
-            if (nb + j < p.n_size) {
-              float x = __uint_as_float(v[j]);
-              if (p.first_touch == 3 /*COPY*/) x += *ap;
-              else if (p.first_touch == 2 /*ADD*/) x += *op + *ap;
-              else if (p.first_touch != 0 /*not ZERO*/) x += *op;
-              if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
-              else if (p.last_touch == 2 /*ADD*/) x += *ap;
-              *op = x;
-            }
-            op += so_n;
-            ap += sa_n;
-          }
-        }
+        store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
       }
       tc_fence_before();
       __syncwarp();

@@ -1,0 +1,372 @@
+// tcgen05 strided binary contraction on CTA pairs (cta_group::2) for sm_100a.
+//
+// A cluster of two CTAs on two SMs computes one 256 (primitive M) x BN
+// (primitive N) output tile with M = 256 tensor-core MMAs issued by the even
+// ("leader") CTA: each CTA stages 128 rows of A and BN/2 rows of B per K block
+// in its own shared memory, the tensor cores of the pair read both halves, and
+// each CTA's TMEM receives its 128 output rows x BN columns. Per SM this loads
+// 128 + BN/2 operand rows per 128 x BN outputs instead of 128 + BN, which is
+// what bounds the one-CTA kernel when its operands stream from L2.
+//
+// Each CTA loads only its own halves (plain TMA tile loads, no multicast); the
+// loads of both CTAs complete on the leader's `full` barrier, whose expected
+// byte count the leader posts for the pair. The leader's MMA issuer releases a
+// ring stage in both CTAs (one commit to each CTA's `empty` barrier) and
+// publishes a finished accumulator to both epilogues the same way. Both
+// epilogues drain their own TMEM and arrive on the leader's `tempty` barrier.
+//
+// Warp roles per CTA: warp 0 = TMA producer, warp 1 = MMA issuer (leader) and
+// TMEM owner (both CTAs allocate with cta_group::2), warps 2..5 = epilogue
+// (fused first / last touch as in the one-CTA kernel). Every wait is bounded;
+// a timeout raises the abort flag in both CTAs and records a device error.
+#include <cuda.h>
+#include "eir_common.cuh"
+#include "eir_params.h"
+#include "eir_kernels.h"
+#include "tc_tile.cuh"
+
+namespace eir {
+
+template <int KIND, int BN, int KSUB>
+struct PairConfig {
+  static constexpr int kEsize = (KIND == kKindBF16) ? 2 : 4;
+  static constexpr int kBM = 128;                  // A rows (output rows) per CTA
+  static constexpr int kBNh = BN / 2;              // B rows per CTA
+  static constexpr int kBK = 128 / kEsize;         // K elements of one 128-byte swizzle row
+  static constexpr int kMmaK = (KIND == kKindBF16) ? 16 : 8;
+  static constexpr int kRowsPerBox = 128 / kEsize; // MN-major: rows per 128B box
+  static constexpr int kASub = kBM * 128;
+  static constexpr int kBSub = kBNh * 128;
+  static constexpr int kABytes = KSUB * kASub;
+  static constexpr int kBBytes = KSUB * kBSub;
+  static constexpr int kStageBytes = kABytes + kBBytes;
+  static constexpr int kMaxStages = 8;
+  static constexpr int kFit = (232448 - 1024 - 512) / kStageBytes;
+  static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
+  static constexpr int kThreads = 192;
+  static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
+  static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
+  static_assert(kStages >= 2, "at least two ring stages");
+  static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
+  static_assert(kSmemBytes <= 232448, "shared memory budget");
+  static_assert(kBNh % 16 == 0, "pair MMA N");
+};
+
+template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+    tc_pair_contract_kernel(const __grid_constant__ CUtensorMap map_a,
+                            const __grid_constant__ CUtensorMap map_b, const TcParams p,
+                            const float *__restrict__ aux, float *__restrict__ out) {
+  using Cfg = PairConfig<KIND, BN, KSUB>;
+  constexpr int S = Cfg::kStages;
+  constexpr int BK = Cfg::kBK;
+  constexpr int BM = Cfg::kBM;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t *smem = reinterpret_cast<uint8_t *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t *sA = smem;                   // S x kABytes
+  uint8_t *sB = sA + S * Cfg::kABytes;  // S x kBBytes
+  uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
+  uint64_t *full = bars;                // S (leader's count both CTAs' bytes)
+  uint64_t *empty = bars + S;           // S
+  uint64_t *tfull = bars + 2 * S;       // 2
+  uint64_t *tempty = bars + 2 * S + 2;  // 2 (leader's: 4 epilogue warps x 2 CTAs)
+  uint64_t *drain = bars + 2 * S + 4;   // 1 (leader: all MMAs done)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+  volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = cluster_ctarank();  // 0 = leader
+  const uint32_t peer = rank ^ 1u;
+  const int64_t pair_id = blockIdx.x >> 1;
+  const int64_t n_pairs = gridDim.x >> 1;
+  const int n_kstages = (p.k_steps + KSUB - 1) / KSUB;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < S; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 8);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 0 && lane == 0) {
+    tma_prefetch_map(&map_a);
+    tma_prefetch_map(&map_b);
+  }
+  if (warp == 1) tmem_alloc_pair(tmem_slot, Cfg::kTmemCols);
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+  const uint32_t peer_abort = mapa_shared(smem_u32((const void *)abort_flag), peer);
+  auto raise_abort = [&](uint32_t code) {
+    if (!*abort_flag) record_error(p.err, code);
+    *abort_flag = 1;
+    st_cluster_u32(peer_abort, 1u);
+  };
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    if (lane == 0) {
+      const uint32_t full_leader = mapa_shared(smem_u32(full), 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int64_t t = pair_id; t < p.total_tiles && ok && !*abort_flag; t += n_pairs) {
+        TileCoord c = decode_tile(p, t);
+        const int rot = k_rotation(t, n_kstages);
+        const int mrow = (int)(c.mt * (2 * BM) + rank * BM);
+        const int nrow = (int)(c.nt * BN + rank * Cfg::kBNh);
+        const SlotCoords sa = slot_coords(p.a_src, c), sb = slot_coords(p.b_src, c);
+        KWalk kw;
+        kw.seek(p, rot * KSUB);
+        for (int js = 0; js < n_kstages; ++js) {
+          int ksg = js + rot;
+          if (ksg >= n_kstages) ksg -= n_kstages;
+          if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
+            ok = false;
+            break;
+          }
+          const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
+          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (Cfg::kASub + Cfg::kBSub));
+          const uint32_t bar = full_leader + 8u * (uint32_t)stage;
+          for (int sub = 0; sub < nsub; ++sub, kw.next(p)) {
+            const int a2 = slot_at(sa, 0, kw.ko0, kw.ko1), a3 = slot_at(sa, 1, kw.ko0, kw.ko1),
+                      a4 = slot_at(sa, 2, kw.ko0, kw.ko1);
+            const int b2 = slot_at(sb, 0, kw.ko0, kw.ko1), b3 = slot_at(sb, 1, kw.ko0, kw.ko1),
+                      b4 = slot_at(sb, 2, kw.ko0, kw.ko1);
+            uint8_t *dA = sA + stage * Cfg::kABytes + sub * Cfg::kASub;
+            uint8_t *dB = sB + stage * Cfg::kBBytes + sub * Cfg::kBSub;
+            const int kcol = kw.kp * BK;
+            if (!A_MN) {
+              tma_load_5d_pair(dA, &map_a, bar, kcol, mrow, a2, a3, a4);
+            } else {
+#pragma unroll
+              for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
+                tma_load_5d_pair(dA + j * BK * 128, &map_a, bar, mrow + j * Cfg::kRowsPerBox, kcol,
+                                 a2, a3, a4);
+            }
+            if (!B_MN) {
+              tma_load_5d_pair(dB, &map_b, bar, kcol, nrow, b2, b3, b4);
+            } else {
+#pragma unroll
+              for (int j = 0; j < Cfg::kBNh / Cfg::kRowsPerBox; ++j)
+                tma_load_5d_pair(dB + j * BK * 128, &map_b, bar, nrow + j * Cfg::kRowsPerBox, kcol,
+                                 b2, b3, b4);
+            }
+          }
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // wait until the MMAs released every stage, so that no commit of the
+      // leader reaches this CTA's barriers after it exits
+      for (int i = 0; i < S && ok && !*abort_flag; ++i) {
+        if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+      if (!ok) raise_abort(kErrTimeoutProducer);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------ MMA issuer (leader)
+    if (lane == 0 && rank == 0) {
+      constexpr uint32_t idesc = make_idesc(KIND, 2 * BM, BN, A_MN, B_MN);
+      constexpr bool kA32 = A_MN && Cfg::kEsize == 4, kB32 = B_MN && Cfg::kEsize == 4;
+      constexpr uint32_t a_lay = kA32 ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t b_lay = kB32 ? kLayoutSw128Base32 : kLayoutSw128;
+      constexpr uint32_t a_sbo = kA32 ? 512 : 1024, b_sbo = kB32 ? 512 : 1024;
+      constexpr uint32_t a_lbo = A_MN ? BK * 128 : 16;
+      constexpr uint32_t b_lbo = B_MN ? BK * 128 : 16;
+      const uint32_t empty_peer = mapa_shared(smem_u32(empty), 1);
+      const uint32_t tfull_peer = mapa_shared(smem_u32(tfull), 1);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      bool ok = true;
+      for (int64_t t = pair_id; t < p.total_tiles && ok; t += n_pairs) {
+        if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
+        const int rot = k_rotation(t, n_kstages);
+        for (int js = 0; js < n_kstages; ++js) {
+          int ksg = js + rot;
+          if (ksg >= n_kstages) ksg -= n_kstages;
+          const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
+          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+#pragma unroll
+          for (int sub = 0; sub < KSUB; ++sub) {
+            if (sub < nsub) {
+              const uint32_t a_base = smem_u32(sA + stage * Cfg::kABytes + sub * Cfg::kASub);
+              const uint32_t b_base = smem_u32(sB + stage * Cfg::kBBytes + sub * Cfg::kBSub);
+#pragma unroll
+              for (int kk = 0; kk < BK / Cfg::kMmaK; ++kk) {
+                const uint32_t a_off = A_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+                const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
+                const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
+                const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
+                const uint32_t accum = (js > 0 || sub > 0 || kk > 0) ? 1u : 0u;
+                if (KIND == kKindBF16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, accum);
+                else umma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
+              }
+            }
+          }
+          umma_commit_pair(smem_u32(&empty[stage]));
+          umma_commit_pair(empty_peer + 8u * (uint32_t)stage);
+          if (++stage == S) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        if (!ok) break;
+        umma_commit_pair(smem_u32(&tfull[acc]));
+        umma_commit_pair(tfull_peer + 8u * (uint32_t)acc);
+        acc ^= 1;
+        if (acc == 0) acc_phase ^= 1u;
+      }
+      // every MMA of this CTA pair has completed before TMEM is released
+      umma_commit_pair(smem_u32(drain));
+      if (!mbar_wait_bounded(drain, 0u, abort_flag) && !*abort_flag) ok = false;
+      if (!ok) raise_abort(kErrTimeoutMma);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int q = warp & 3;  // TMEM lane quadrant this warp may access
+    const int row = q * 32 + lane;
+    const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
+    const int fast = epilogue_kind(p);
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int64_t t = pair_id; t < p.total_tiles; t += n_pairs) {
+      TileCoord c = decode_tile(p, t);
+      if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
+        if (lane == 0) raise_abort(kErrTimeoutEpilogue);
+        break;
+      }
+      tc_fence_after();
+      const int64_t m = c.mt * (2 * BM) + rank * BM + row;
+      const bool mval = m < p.m_size;
+      int64_t ob = m * p.so_m, ab = m * p.sa_m;
+#pragma unroll
+      for (int i = 0; i < kMaxTileLoops; ++i) {
+        ob += c.l[i] * p.loop_so[i];
+        ab += c.l[i] * p.loop_sa[i];
+      }
+      const int64_t n0 = c.nt * BN;
+      const int64_t so_n = p.so_n, sa_n = p.sa_n;
+#pragma unroll 1
+      for (int ch = 0; ch < BN / 32; ++ch) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
+        tmem_ld_wait();
+        if (!mval) continue;
+        const int64_t nb = n0 + ch * 32;
+        store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(tempty_leader + 8u * (uint32_t)acc);
+      acc ^= 1;
+      if (acc == 0) acc_phase ^= 1u;
+    }
+  }
+
+  // After an abort, copies or commits issued before it may still be landing in
+  // this CTA's shared memory: give them time before the CTA can exit.
+  if (threadIdx.x == 0 && *abort_flag) {
+    for (int i = 0; i < 1000; ++i) __nanosleep(1000);
+  }
+  __syncwarp();
+  tc_fence_before();
+  cluster_sync();  // both CTAs done: no remote arrive or TMEM read is outstanding
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, Cfg::kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
+static cudaError_t launch_pair_t(CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
+                                 float const *aux, float *out, cudaStream_t st) {
+  using Cfg = PairConfig<KIND, BN, KSUB>;
+  auto kern = tc_pair_contract_kernel<KIND, BN, KSUB, A_MN, B_MN>;
+  static int max_clusters[32] = {0};  // per device: co-resident clusters of this instantiation
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int mc = dev < 32 ? max_clusters[dev] : 0;
+  if (mc == 0) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         Cfg::kSmemBytes);
+    if (e != cudaSuccess) return e;
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(2, 1, 1);
+    cfg.blockDim = dim3(Cfg::kThreads, 1, 1);
+    cfg.dynamicSmemBytes = Cfg::kSmemBytes;
+    e = cudaOccupancyMaxActiveClusters(&mc, kern, &cfg);
+    if (e != cudaSuccess) return e;
+    if (mc < 1) return cudaErrorInvalidConfiguration;
+    if (dev < 32) max_clusters[dev] = mc;
+  }
+  int64_t pairs = p.total_tiles < mc ? p.total_tiles : mc;
+  if (pairs < 1) return cudaSuccess;
+  kern<<<(unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, st>>>(ma, mb, p, aux, out);
+  return cudaGetLastError();
+}
+
+template <int KIND, int BN, int KSUB>
+static cudaError_t launch_pair_major(bool a_mn, bool b_mn, CUtensorMap const &ma,
+                                     CUtensorMap const &mb, TcParams const &p, float const *aux,
+                                     float *out, cudaStream_t st) {
+  if (!a_mn && !b_mn) return launch_pair_t<KIND, BN, KSUB, false, false>(ma, mb, p, aux, out, st);
+  if (!a_mn && b_mn) return launch_pair_t<KIND, BN, KSUB, false, true>(ma, mb, p, aux, out, st);
+  if (a_mn && !b_mn) return launch_pair_t<KIND, BN, KSUB, true, false>(ma, mb, p, aux, out, st);
+  return launch_pair_t<KIND, BN, KSUB, true, true>(ma, mb, p, aux, out, st);
+}
+
+cudaError_t launch_tc_pair_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
+                                    CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
+                                    float const *aux, float *out, cudaStream_t st) {
+  if (kind == kKindBF16 && bn == 256 && ksub == 1)
+    return launch_pair_major<kKindBF16, 256, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindBF16 && bn == 256 && ksub == 2)
+    return launch_pair_major<kKindBF16, 256, 2>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindBF16 && bn == 128 && ksub == 2)
+    return launch_pair_major<kKindBF16, 128, 2>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindBF16 && bn == 128 && ksub == 1)
+    return launch_pair_major<kKindBF16, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindTF32 && bn == 256 && ksub == 1)
+    return launch_pair_major<kKindTF32, 256, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindTF32 && bn == 256 && ksub == 2)
+    return launch_pair_major<kKindTF32, 256, 2>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindTF32 && bn == 128 && ksub == 2)
+    return launch_pair_major<kKindTF32, 128, 2>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKindTF32 && bn == 128 && ksub == 1)
+    return launch_pair_major<kKindTF32, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  return cudaErrorInvalidValue;
+}
+
+}  // namespace eir

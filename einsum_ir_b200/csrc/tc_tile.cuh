@@ -1,0 +1,169 @@
+// Tile scheduling and epilogue pieces shared by the tcgen05 contraction
+// kernels (one CTA per tile in kernels_tc.cu, CTA pairs in kernels_tc2.cu).
+#pragma once
+
+#include <cstdint>
+#include "eir_params.h"
+
+namespace eir {
+
+enum { kKindBF16 = 0, kKindTF32 = 1, kKind3xTF32 = 2 };
+
+// instruction descriptor for kind::f16 (bf16) / kind::tf32, FP32 accumulate
+__host__ __device__ constexpr uint32_t make_idesc(int kind, int m, int n, bool a_mn, bool b_mn) {
+  uint32_t fmt = (kind == kKindBF16) ? 1u : 2u;  // BF16 = 1, TF32 = 2
+  return (1u << 4)                               // D format F32
+         | (fmt << 7) | (fmt << 10)              // A / B format
+         | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
+         | ((uint32_t)(n >> 3) << 17) | ((uint32_t)(m >> 4) << 24);
+}
+
+struct TileCoord {
+  int64_t mt, nt;
+  int64_t l[kMaxTileLoops];
+};
+
+// tile index -> (M tile, N tile, tile-loop indices); M/N tiles in groups of group_m M tiles
+__device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
+  TileCoord c;
+  const int64_t mn = (int64_t)p.m_tiles * p.n_tiles;
+  int64_t u = t % mn;
+  t /= mn;
+  const int64_t gsz_full = (int64_t)p.group_m * p.n_tiles;
+  const int64_t g = u / gsz_full;
+  const int64_t first_m = g * p.group_m;
+  const int64_t rem_m = p.m_tiles - first_m;
+  const int64_t gm = rem_m < p.group_m ? rem_m : p.group_m;
+  const int64_t r = u - g * gsz_full;
+  c.mt = first_m + r % gm;
+  c.nt = r / gm;
+#pragma unroll
+  for (int i = 0; i < kMaxTileLoops; ++i) {
+    if (i < p.n_loops) {
+      c.l[i] = t % p.loop_size[i];
+      t /= p.loop_size[i];
+    } else {
+      c.l[i] = 0;
+    }
+  }
+  return c;
+}
+
+__device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, TileCoord const &c) {
+  switch (src) {
+    case kSrcKo0: return (int)ko0;
+    case kSrcKo1: return (int)ko1;
+    case kSrcLoop0: return (int)c.l[0];
+    case kSrcLoop0 + 1: return (int)c.l[1];
+    case kSrcLoop0 + 2: return (int)c.l[2];
+    case kSrcLoop0 + 3: return (int)c.l[3];
+    default: return 0;
+  }
+}
+
+// TMA coordinates 2..4 of one operand for one tile: the tile-loop indices are
+// fixed per tile, the outer K indices (ko0, ko1) change along the K walk.
+struct SlotCoords {
+  int base[3];
+  int ko0_mask, ko1_mask;  // bit j: coordinate 2 + j is ko0 / ko1
+};
+
+__device__ __forceinline__ SlotCoords slot_coords(int8_t const (&src)[5], TileCoord const &c) {
+  SlotCoords s;
+  s.ko0_mask = s.ko1_mask = 0;
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    s.base[j] = src_coord(src[2 + j], 0, 0, c);
+    if (src[2 + j] == kSrcKo0) s.ko0_mask |= 1 << j;
+    if (src[2 + j] == kSrcKo1) s.ko1_mask |= 1 << j;
+  }
+  return s;
+}
+
+__device__ __forceinline__ int slot_at(SlotCoords const &s, int j, int ko0, int ko1) {
+  return s.base[j] + (((s.ko0_mask >> j) & 1) ? ko0 : 0) + (((s.ko1_mask >> j) & 1) ? ko1 : 0);
+}
+
+// Position (kp, ko0, ko1) of K block ks = kp + kp_blocks * (ko0 + ko_size0 * ko1),
+// advanced without divisions: the producer thread issues every TMA load of
+// the CTA, so its per-K-block instruction count bounds the operand rate.
+struct KWalk {
+  int ks, kp, ko0, ko1;
+  __device__ __forceinline__ void seek(TcParams const &p, int k) {
+    ks = k;
+    kp = k % p.kp_blocks;
+    const int r = k / p.kp_blocks;
+    ko0 = r % (int)p.ko_size[0];
+    ko1 = r / (int)p.ko_size[0];
+  }
+  // next K block; the walk wraps from the last block to block 0
+  __device__ __forceinline__ void next(TcParams const &p) {
+    if (++ks == p.k_steps) {
+      ks = kp = ko0 = ko1 = 0;
+    } else if (++kp == p.kp_blocks) {
+      kp = 0;
+      if (++ko0 == (int)p.ko_size[0]) {
+        ko0 = 0;
+        ++ko1;
+      }
+    }
+  }
+};
+
+// Start offset (in stages) of a tile's K walk. Tiles running at the same time
+// start at different K positions so they do not all fetch the same operand
+// lines at once (the sum over K is order independent up to FP32 rounding).
+// Producer and MMA issuer only need to agree on the order of stages; the first
+// MMA of a tile's walk always initialises the accumulator.
+__device__ __forceinline__ int k_rotation(int64_t t, int n_stages) {
+  if (n_stages <= 1) return 0;
+  return (int)((t * 7) % n_stages);
+}
+
+// Epilogue variant of a plan: 0 = ZERO first touch and no last touch, 1 = COPY
+// (bias) first touch with no last touch or RELU, 2 = anything else.
+__device__ __forceinline__ int epilogue_kind(TcParams const &p) {
+  return (p.first_touch == 0 && p.last_touch == 99) ? 0
+       : (p.first_touch == 3 && (p.last_touch == 99 || p.last_touch == 1)) ? 1 : 2;
+}
+
+// Writes 32 consecutive accumulator columns (output columns nb .. nb+31) of one
+// output row with the fused first / last touch. `op` / `ap` point at column nb
+// of the output / aux row; the full-chunk fast paths walk them by increments.
+__device__ __forceinline__ void store_chunk(TcParams const &p, uint32_t const (&v)[32], float *op,
+                                            const float *ap, int64_t nb, int64_t so_n, int64_t sa_n,
+                                            int fast) {
+  const bool relu = p.last_touch == 1;
+  if (fast == 0 && nb + 32 <= p.n_size) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      *op = __uint_as_float(v[j]);
+      op += so_n;
+    }
+  } else if (fast == 1 && nb + 32 <= p.n_size) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      float x = __uint_as_float(v[j]) + __ldg(ap);
+      *op = relu ? fmaxf(x, 0.0f) : x;
+      op += so_n;
+      ap += sa_n;
+    }
+  } else {
+#pragma unroll 4
+    for (int j = 0; j < 32; ++j) {
+      if (nb + j < p.n_size) {
+        float x = __uint_as_float(v[j]);
+        if (p.first_touch == 3 /*COPY*/) x += *ap;
+        else if (p.first_touch == 2 /*ADD*/) x += *op + *ap;
+        else if (p.first_touch != 0 /*not ZERO*/) x += *op;
+        if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
+        else if (p.last_touch == 2 /*ADD*/) x += *ap;
+        *op = x;
+      }
+      op += so_n;
+      ap += sa_n;
+    }
+  }
+}
+
+}  // namespace eir

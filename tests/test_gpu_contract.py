@@ -43,10 +43,17 @@ def _np_in(t):
 
 def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
              last=cabi.KTYPE_UNDEFINED, aux_outer=None, flags=0, seed=0, expect_family=None,
-             tf32_general=False, tc_min_ops="0"):
+             tf32_general=False, tc_min_ops="0", pair=None, bn=None, ksub=None):
+    """pair / bn / ksub force the tensor-core tile shape (CTA pair or one CTA,
+    BN, K blocks per stage); None leaves the planner's choice."""
     import torch
     os.environ["EIR_TC_MIN_OPS"] = tc_min_ops
     os.environ["EIR_TC_MIN_UTIL"] = "0"
+    for var, val in (("EIR_TC_PAIR", pair), ("EIR_TC_BN", bn), ("EIR_TC_KSUB", ksub)):
+        if val is None:
+            os.environ.pop(var, None)
+        else:
+            os.environ[var] = str(val)
     il, ir, io, names = binary.parse_binary(expr)
     sz = {i: sizes[c] for i, c in enumerate(names)}
     aux_sizes = None
@@ -121,25 +128,61 @@ def test_tc_parity(cuda, expr, sizes, dtype):
     run_case(cuda, expr, sizes, dtype, expect_family=TC)
 
 
+def _m_size(expr, sizes):
+    """size of the primitive M dim the planner picks: the output's fastest M dim"""
+    il, ir, io, names = binary.parse_binary(expr)
+    return sizes[names[[i for i in io if i in il][-1]]]
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("expr,sizes,dtype", [c for c in TC_CASES if c[2] != "fp32"])
+def test_tc_parity_tile_shapes(cuda, expr, sizes, dtype, pair):
+    """Every BF16 / TF32 case on the one-CTA kernel and on CTA pairs (cta_group::2)."""
+    plan, _ = run_case(cuda, expr, sizes, dtype, expect_family=TC, pair=pair)
+    assert ("pair" in plan.describe()) == (pair == 1 and _m_size(expr, sizes) > 128), plan.describe()
+
+
+PAIR_CASES = [
+    # M = 300: the second pair tile's odd CTA reads only rows past the end (TMA zero fill)
+    ("mk,nk->nm", dict(m=300, n=200, k=96), "bf16", 256, 2),
+    ("mk,nk->nm", dict(m=300, n=200, k=96), "bf16", 128, 1),
+    ("km,kn->nm", dict(m=384, n=136, k=72), "bf16", 128, 2),
+    ("km,kn->nm", dict(m=260, n=520, k=40), "tf32", 256, 1),
+    ("mk,kn->nm", dict(m=512, n=256, k=256), "tf32", 128, 1),
+    # several tiles per pair (persistent loop, accumulator double buffering)
+    ("cmk,cnk->cnm", dict(c=40, m=512, n=512, k=128), "bf16", 256, 2),
+    ("akmj,njk->anm", dict(a=4, k=8, m=512, j=64, n=512), "bf16", 256, 2),
+]
+
+
+@pytest.mark.parametrize("expr,sizes,dtype,bn,ksub", PAIR_CASES)
+def test_tc_pair_shapes(cuda, expr, sizes, dtype, bn, ksub):
+    plan, _ = run_case(cuda, expr, sizes, dtype, expect_family=TC, pair=1, bn=bn, ksub=ksub)
+    d = plan.describe()
+    assert "pair" in d and f"BN={bn} KSUB={ksub}" in d, d
+
+
 def test_tc_tf32_general_inputs(cuda):
     run_case(cuda, "km,nk->nm", dict(m=256, n=256, k=256), "tf32", tf32_general=True,
              expect_family=TC)
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "bf16", "tf32"])
-def test_tc_mlp_layer_bias_relu(cuda, dtype):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_tc_mlp_layer_bias_relu(cuda, dtype, pair):
     # bench_mlp hidden layer: COPY bias (broadcast over b) first touch, RELU last touch
     run_case(cuda, "io,bi->bo", dict(b=256, i=192, o=320), dtype, first=cabi.KTYPE_COPY,
-             last=cabi.KTYPE_RELU, aux_outer="b", expect_family=TC)
+             last=cabi.KTYPE_RELU, aux_outer="b", expect_family=TC, pair=pair)
 
 
 @pytest.mark.parametrize("first,last", [(cabi.KTYPE_UNDEFINED, cabi.KTYPE_UNDEFINED),
                                         (cabi.KTYPE_ADD, cabi.KTYPE_UNDEFINED),
                                         (cabi.KTYPE_ZERO, cabi.KTYPE_ADD),
                                         (cabi.KTYPE_COPY, cabi.KTYPE_ADD)])
-def test_tc_touch_kernels(cuda, first, last):
+@pytest.mark.parametrize("pair", [0, 1])
+def test_tc_touch_kernels(cuda, first, last, pair):
     run_case(cuda, "mk,nk->nm", dict(m=160, n=96, k=64), "bf16", first=first, last=last,
-             aux_outer="n", expect_family=TC)
+             aux_outer="n", expect_family=TC, pair=pair)
 
 
 DMMA = cabi.FAMILY_DMMA
