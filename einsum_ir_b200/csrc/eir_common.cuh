@@ -103,6 +103,18 @@ __device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, v
   return ok != 0;
 }
 
+// ---- programmatic dependent launch ---------------------------------------
+// A kernel launched with programmatic stream serialisation may start while
+// the previous kernel of the stream is still running; pdl_wait() blocks until
+// that kernel has completed and its memory is visible, so every thread calls
+// it before its first global memory access. Kernels launched without the
+// attribute return from it at once. pdl_launch_dependents() lets the next
+// kernel of the stream start its prologue early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 __device__ __forceinline__ void record_error(uint32_t *err, uint32_t code) {
   if (err != nullptr) atomicCAS(err, 0u, code);
 }

@@ -14,6 +14,7 @@
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
+#include "eir_launch.h"
 
 namespace eir {
 
@@ -111,6 +112,8 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
     fence_barrier_init();
   }
   __syncthreads();
+  pdl_launch_dependents();
+  pdl_wait();  // operands / output may come from the previous kernel of the stream
   const int k_steps = p.k_steps;
 
   if (warp == 0) {
@@ -260,8 +263,8 @@ static cudaError_t launch_dmma_t(CUtensorMap const &ma, CUtensorMap const &mb, T
   }
   int64_t grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (grid < 1) return cudaSuccess;
-  kern<<<(unsigned)grid, kDmmaThreads, kDmmaSmem, st>>>(ma, mb, p, aux, out);
-  return cudaGetLastError();
+  return launch_kernel(kern, dim3((unsigned)grid), dim3(kDmmaThreads), kDmmaSmem, st, ma, mb, p, aux,
+                       out);
 }
 
 cudaError_t launch_dmma_contract(bool a_mn, bool b_mn, CUtensorMap const &ma, CUtensorMap const &mb,

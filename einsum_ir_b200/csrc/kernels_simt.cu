@@ -12,6 +12,7 @@
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
+#include "eir_launch.h"
 
 namespace eir {
 
@@ -62,6 +63,8 @@ __global__ void __launch_bounds__(256)
   __shared__ int64_t col_r[BN], col_o[BN], col_a[BN];
   __shared__ int64_t k_l[BK], k_r[BK];
 
+  pdl_launch_dependents();
+  pdl_wait();
   const int tid = threadIdx.x;
   const int tx = tid & 15, ty = tid >> 4;
   int64_t bid = blockIdx.x;
@@ -179,10 +182,9 @@ static cudaError_t launch_simt_t(SimtParams const &p, void const *l, void const 
   int64_t blocks = p.m_tiles * p.n_tiles * p.c.total;
   if (blocks <= 0) return cudaSuccess;
   if (blocks > 0x7fffffffLL) return cudaErrorInvalidConfiguration;
-  simt_contract_kernel<TL, TR, TO, TA><<<(unsigned)blocks, 256, 0, st>>>(
-      p, static_cast<TL const *>(l), static_cast<TR const *>(r), static_cast<TO const *>(aux),
-      static_cast<TO *>(out));
-  return cudaGetLastError();
+  return launch_kernel(simt_contract_kernel<TL, TR, TO, TA>, dim3((unsigned)blocks), dim3(256), 0, st,
+                       p, static_cast<TL const *>(l), static_cast<TR const *>(r),
+                       static_cast<TO const *>(aux), static_cast<TO *>(out));
 }
 
 // dtypes: 0 = FP32, 1 = FP64, 2 = BF16 (values of the C-ABI enum)
@@ -211,6 +213,8 @@ __global__ void __launch_bounds__(256)
   struct alignas(sizeof(T) * V) Vec {
     T v[V];
   };
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t n0v = p.size[0] / V;
   const int64_t total = p.rows * n0v;
   for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
@@ -241,6 +245,8 @@ __global__ void __launch_bounds__(256)
   __shared__ T tile[TS][TS + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   const int td = p.tdim_in;
+  pdl_launch_dependents();
+  pdl_wait();
   const int64_t s0 = p.size[0], st = p.size[td];
   const int64_t t0 = (s0 + TS - 1) / TS, tt = (st + TS - 1) / TS;
   const int64_t nblk = t0 * tt * p.batch;
@@ -282,6 +288,7 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
   if (p.total == 0) return cudaSuccess;
   const T *i = static_cast<T const *>(in);
   T *o = static_cast<T *>(out);
+  cudaError_t e = cudaSuccess;
   if (p.mode == 0) {
     int64_t work = p.total / p.vec;
     int64_t blocks = (work + 255) / 256;
@@ -289,10 +296,10 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
     switch (p.vec) {
-      case 1: permute_copy_kernel<T, 1><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
-      case 2: permute_copy_kernel<T, 2><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
-      case 4: permute_copy_kernel<T, 4><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
-      case 8: permute_copy_kernel<T, 8><<<(unsigned)blocks, 256, 0, st>>>(p, i, o); break;
+      case 1: e = launch_kernel(permute_copy_kernel<T, 1>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
+      case 2: e = launch_kernel(permute_copy_kernel<T, 2>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
+      case 4: e = launch_kernel(permute_copy_kernel<T, 4>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
+      case 8: e = launch_kernel(permute_copy_kernel<T, 8>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
       default: return cudaErrorInvalidValue;
     }
   } else {
@@ -300,9 +307,9 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
     int64_t cap = (int64_t)num_sms * 8;
     int64_t blocks = nblk < cap ? nblk : cap;
     if (blocks < 1) blocks = 1;
-    permute_transpose_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(p, i, o);
+    e = launch_kernel(permute_transpose_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
   }
-  return cudaGetLastError();
+  return e;
 }
 
 cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,

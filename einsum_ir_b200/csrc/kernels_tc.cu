@@ -29,6 +29,7 @@
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
+#include "eir_launch.h"
 #include "tc_tile.cuh"
 
 namespace eir {
@@ -125,6 +126,8 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();  // operands / output may come from the previous kernel of the stream
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -136,6 +139,24 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         const int rot = k_rotation(t, n_kstages);
         const int mrow = (int)(c.mt * BM), nrow = (int)(c.nt * BN);
         const SlotCoords sa = slot_coords(p.a_src, c), sb = slot_coords(p.b_src, c);
+        // the TMA boxes of one K block into a ring stage
+        auto k_block = [&](KWalk const &w, uint8_t *dA, uint8_t *dB, uint64_t *bar) {
+          const int a2 = slot_at(sa, 0, w.ko0, w.ko1), a3 = slot_at(sa, 1, w.ko0, w.ko1),
+                    a4 = slot_at(sa, 2, w.ko0, w.ko1);
+          const int b2 = slot_at(sb, 0, w.ko0, w.ko1), b3 = slot_at(sb, 1, w.ko0, w.ko1),
+                    b4 = slot_at(sb, 2, w.ko0, w.ko1);
+          const int kcol = w.kp * BK;
+#pragma unroll
+          for (int j = 0; j < (A_MN ? BM / Cfg::kRowsPerBox : 1); ++j) {
+            const int x = A_MN ? mrow + j * Cfg::kRowsPerBox : kcol, y = A_MN ? kcol : mrow;
+            tma_load_5d(dA + j * BK * 128, &map_a, bar, x, y, a2, a3, a4);
+          }
+#pragma unroll
+          for (int j = 0; j < (B_MN ? BN / Cfg::kRowsPerBox : 1); ++j) {
+            const int x = B_MN ? nrow + j * Cfg::kRowsPerBox : kcol, y = B_MN ? kcol : nrow;
+            tma_load_5d(dB + j * BK * 128, &map_b, bar, x, y, b2, b3, b4);
+          }
+        };
         KWalk kw;
         kw.seek(p, rot * KSUB);
         for (int js = 0; js < n_kstages; ++js) {
@@ -148,31 +169,9 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           }
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
           mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
-          for (int sub = 0; sub < nsub; ++sub, kw.next(p)) {
-            const int a2 = slot_at(sa, 0, kw.ko0, kw.ko1), a3 = slot_at(sa, 1, kw.ko0, kw.ko1),
-                      a4 = slot_at(sa, 2, kw.ko0, kw.ko1);
-            const int b2 = slot_at(sb, 0, kw.ko0, kw.ko1), b3 = slot_at(sb, 1, kw.ko0, kw.ko1),
-                      b4 = slot_at(sb, 2, kw.ko0, kw.ko1);
-            uint8_t *dA = sA + stage * Cfg::kABytes + sub * Cfg::kASub;
-            uint8_t *dB = sB + stage * Cfg::kBBytes + sub * Cfg::kBSub;
-            const int kcol = kw.kp * BK;
-            if (!A_MN) {
-              tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
-            } else {
-#pragma unroll
-              for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
-                tma_load_5d(dA + j * BK * 128, &map_a, &full[stage], mrow + j * Cfg::kRowsPerBox,
-                            kcol, a2, a3, a4);
-            }
-            if (!B_MN) {
-              tma_load_5d(dB, &map_b, &full[stage], kcol, nrow, b2, b3, b4);
-            } else {
-#pragma unroll
-              for (int j = 0; j < BN / Cfg::kRowsPerBox; ++j)
-                tma_load_5d(dB + j * BK * 128, &map_b, &full[stage], nrow + j * Cfg::kRowsPerBox,
-                            kcol, b2, b3, b4);
-            }
-          }
+          for (int sub = 0; sub < nsub; ++sub, kw.next(p))
+            k_block(kw, sA + stage * Cfg::kABytes + sub * Cfg::kASub,
+                    sB + stage * Cfg::kBBytes + sub * Cfg::kBSub, &full[stage]);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -357,8 +356,8 @@ static cudaError_t launch_tc_t(CUtensorMap const &ma, CUtensorMap const &mb, TcP
   }
   int64_t grid = p.total_tiles < num_sms ? p.total_tiles : num_sms;
   if (grid < 1) return cudaSuccess;
-  kern<<<(unsigned)grid, Cfg::kThreads, Cfg::kSmemBytes, st>>>(ma, mb, p, aux, out);
-  return cudaGetLastError();
+  return launch_kernel(kern, dim3((unsigned)grid), dim3(Cfg::kThreads), Cfg::kSmemBytes, st, ma, mb,
+                       p, aux, out);
 }
 
 template <int KIND, int BN, int KSUB>

@@ -16,13 +16,15 @@
 // epilogues drain their own TMEM and arrive on the leader's `tempty` barrier.
 //
 // Warp roles per CTA: warp 0 = TMA producer, warp 1 = MMA issuer (leader) and
-// TMEM owner (both CTAs allocate with cta_group::2), warps 2..5 = epilogue
-// (fused first / last touch as in the one-CTA kernel). Every wait is bounded;
+// TMEM owner (both CTAs allocate with cta_group::2), warps 2..9 = epilogue, two
+// per TMEM lane quadrant with half of the columns each (fused first / last
+// touch as in the one-CTA kernel). Every wait is bounded;
 // a timeout raises the abort flag in both CTAs and records a device error.
 #include <cuda.h>
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
+#include "eir_launch.h"
 #include "tc_tile.cuh"
 
 namespace eir {
@@ -43,7 +45,8 @@ struct PairConfig {
   static constexpr int kMaxStages = 8;
   static constexpr int kFit = (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
-  static constexpr int kThreads = 192;
+  static constexpr int kEpiWarps = 8;             // 2 per TMEM lane quadrant, half the columns each
+  static constexpr int kThreads = 32 * (2 + kEpiWarps);
   static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
   static_assert(kStages >= 2, "at least two ring stages");
@@ -53,7 +56,7 @@ struct PairConfig {
 };
 
 template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN, KSUB>::kThreads, 1)
     tc_pair_contract_kernel(const __grid_constant__ CUtensorMap map_a,
                             const __grid_constant__ CUtensorMap map_b, const TcParams p,
                             const float *__restrict__ aux, float *__restrict__ out) {
@@ -71,7 +74,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   uint64_t *full = bars;                // S (leader's count both CTAs' bytes)
   uint64_t *empty = bars + S;           // S
   uint64_t *tfull = bars + 2 * S;       // 2
-  uint64_t *tempty = bars + 2 * S + 2;  // 2 (leader's: 4 epilogue warps x 2 CTAs)
+  uint64_t *tempty = bars + 2 * S + 2;  // 2 (leader's: epilogue warps of both CTAs)
   uint64_t *drain = bars + 2 * S + 4;   // 1 (leader: all MMAs done)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -91,7 +94,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 8);
+      mbar_init(&tempty[a], 2 * Cfg::kEpiWarps);
     }
     mbar_init(drain, 1);
     *abort_flag = 0;
@@ -106,6 +109,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
   cluster_sync();  // barriers of both CTAs initialised before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+  pdl_launch_dependents();
+  pdl_wait();  // operands / output may come from the previous kernel of the stream
   const uint32_t peer_abort = mapa_shared(smem_u32((const void *)abort_flag), peer);
   auto raise_abort = [&](uint32_t code) {
     if (!*abort_flag) record_error(p.err, code);
@@ -126,6 +131,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         const int mrow = (int)(c.mt * (2 * BM) + rank * BM);
         const int nrow = (int)(c.nt * BN + rank * Cfg::kBNh);
         const SlotCoords sa = slot_coords(p.a_src, c), sb = slot_coords(p.b_src, c);
+        // the TMA boxes of one K block of this CTA's operand halves
+        auto k_block = [&](KWalk const &w, uint8_t *dA, uint8_t *dB, uint32_t bar) {
+          const int a2 = slot_at(sa, 0, w.ko0, w.ko1), a3 = slot_at(sa, 1, w.ko0, w.ko1),
+                    a4 = slot_at(sa, 2, w.ko0, w.ko1);
+          const int b2 = slot_at(sb, 0, w.ko0, w.ko1), b3 = slot_at(sb, 1, w.ko0, w.ko1),
+                    b4 = slot_at(sb, 2, w.ko0, w.ko1);
+          const int kcol = w.kp * BK;
+#pragma unroll
+          for (int j = 0; j < (A_MN ? BM / Cfg::kRowsPerBox : 1); ++j) {
+            const int x = A_MN ? mrow + j * Cfg::kRowsPerBox : kcol, y = A_MN ? kcol : mrow;
+            tma_load_5d_pair(dA + j * BK * 128, &map_a, bar, x, y, a2, a3, a4);
+          }
+#pragma unroll
+          for (int j = 0; j < (B_MN ? Cfg::kBNh / Cfg::kRowsPerBox : 1); ++j) {
+            const int x = B_MN ? nrow + j * Cfg::kRowsPerBox : kcol, y = B_MN ? kcol : nrow;
+            tma_load_5d_pair(dB + j * BK * 128, &map_b, bar, x, y, b2, b3, b4);
+          }
+        };
         KWalk kw;
         kw.seek(p, rot * KSUB);
         for (int js = 0; js < n_kstages; ++js) {
@@ -138,31 +161,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
           if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (Cfg::kASub + Cfg::kBSub));
           const uint32_t bar = full_leader + 8u * (uint32_t)stage;
-          for (int sub = 0; sub < nsub; ++sub, kw.next(p)) {
-            const int a2 = slot_at(sa, 0, kw.ko0, kw.ko1), a3 = slot_at(sa, 1, kw.ko0, kw.ko1),
-                      a4 = slot_at(sa, 2, kw.ko0, kw.ko1);
-            const int b2 = slot_at(sb, 0, kw.ko0, kw.ko1), b3 = slot_at(sb, 1, kw.ko0, kw.ko1),
-                      b4 = slot_at(sb, 2, kw.ko0, kw.ko1);
-            uint8_t *dA = sA + stage * Cfg::kABytes + sub * Cfg::kASub;
-            uint8_t *dB = sB + stage * Cfg::kBBytes + sub * Cfg::kBSub;
-            const int kcol = kw.kp * BK;
-            if (!A_MN) {
-              tma_load_5d_pair(dA, &map_a, bar, kcol, mrow, a2, a3, a4);
-            } else {
-#pragma unroll
-              for (int j = 0; j < BM / Cfg::kRowsPerBox; ++j)
-                tma_load_5d_pair(dA + j * BK * 128, &map_a, bar, mrow + j * Cfg::kRowsPerBox, kcol,
-                                 a2, a3, a4);
-            }
-            if (!B_MN) {
-              tma_load_5d_pair(dB, &map_b, bar, kcol, nrow, b2, b3, b4);
-            } else {
-#pragma unroll
-              for (int j = 0; j < Cfg::kBNh / Cfg::kRowsPerBox; ++j)
-                tma_load_5d_pair(dB + j * BK * 128, &map_b, bar, nrow + j * Cfg::kRowsPerBox, kcol,
-                                 b2, b3, b4);
-            }
-          }
+          for (int sub = 0; sub < nsub; ++sub, kw.next(p))
+            k_block(kw, sA + stage * Cfg::kABytes + sub * Cfg::kASub,
+                    sB + stage * Cfg::kBBytes + sub * Cfg::kBSub, bar);
           if (++stage == S) {
             stage = 0;
             phase ^= 1u;
@@ -256,6 +257,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
+    constexpr int kCols = BN * 4 / Cfg::kEpiWarps;   // accumulator columns of this warp
+    const int col0 = ((warp - 2) >> 2) * kCols;
     const uint32_t tempty_leader = mapa_shared(smem_u32(tempty), 0);
     const int fast = epilogue_kind(p);
     int acc = 0;
@@ -275,12 +278,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(192, 1)
         ob += c.l[i] * p.loop_so[i];
         ab += c.l[i] * p.loop_sa[i];
       }
-      const int64_t n0 = c.nt * BN;
+      const int64_t n0 = c.nt * BN + col0;
       const int64_t so_n = p.so_n, sa_n = p.sa_n;
 #pragma unroll 1
-      for (int ch = 0; ch < BN / 32; ++ch) {
+      for (int ch = 0; ch < kCols / 32; ++ch) {
         uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + ch * 32), v);
+        tmem_ld_32x32b_x32(tmem_base + ((uint32_t)(q * 32) << 16) + (uint32_t)(acc * BN + col0 + ch * 32), v);
         tmem_ld_wait();
         if (!mval) continue;
         const int64_t nb = n0 + ch * 32;
@@ -333,8 +336,8 @@ static cudaError_t launch_pair_t(CUtensorMap const &ma, CUtensorMap const &mb, T
   }
   int64_t pairs = p.total_tiles < mc ? p.total_tiles : mc;
   if (pairs < 1) return cudaSuccess;
-  kern<<<(unsigned)(2 * pairs), Cfg::kThreads, Cfg::kSmemBytes, st>>>(ma, mb, p, aux, out);
-  return cudaGetLastError();
+  return launch_kernel(kern, dim3((unsigned)(2 * pairs)), dim3(Cfg::kThreads), Cfg::kSmemBytes, st,
+                       ma, mb, p, aux, out);
 }
 
 template <int KIND, int BN, int KSUB>
