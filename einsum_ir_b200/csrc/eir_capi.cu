@@ -569,6 +569,10 @@ bool try_tc(eir_plan *p, std::string *why) {
   t.k_steps = (int32_t)ksteps;
   t.total_tiles = (int64_t)t.m_tiles * t.n_tiles;
   for (int j = 0; j < t.n_loops; ++j) t.total_tiles *= t.loop_size[j];
+  if (t.total_tiles >= (int64_t(1) << 31)) {  // the kernels index tiles in 32 bits
+    *why = "too many output tiles";
+    return false;
+  }
   t.first_touch = p->first;
   t.last_touch = p->last;
   t.group_m = (int32_t)std::max<int64_t>(1, env_int("EIR_TC_GROUP_M", 16));

@@ -100,6 +100,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
     *abort_flag = 0;
     fence_barrier_init();
   }
+  // the producer's first-tile set-up (kernel parameter loads, index
+  // arithmetic) overlaps the rest of the prologue
+  ProducerTile first_tile{};
+  if (threadIdx.x == 0 && pair_id < p.total_tiles)
+    first_tile = producer_tile<KSUB>(p, pair_id, n_kstages, 2 * BM, (int)rank * BM, BN,
+                                     (int)rank * Cfg::kBNh);
   if (warp == 0 && lane == 0) {
     tma_prefetch_map(&map_a);
     tma_prefetch_map(&map_b);
@@ -126,31 +132,30 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       uint32_t phase = 0;
       bool ok = true;
       for (int64_t t = pair_id; t < p.total_tiles && ok && !*abort_flag; t += n_pairs) {
-        TileCoord c = decode_tile(p, t);
-        const int rot = k_rotation(t, n_kstages);
-        const int mrow = (int)(c.mt * (2 * BM) + rank * BM);
-        const int nrow = (int)(c.nt * BN + rank * Cfg::kBNh);
-        const SlotCoords sa = slot_coords(p.a_src, c), sb = slot_coords(p.b_src, c);
+        const ProducerTile pt = t == pair_id
+                                    ? first_tile
+                                    : producer_tile<KSUB>(p, t, n_kstages, 2 * BM, (int)rank * BM, BN,
+                                                          (int)rank * Cfg::kBNh);
         // the TMA boxes of one K block of this CTA's operand halves
         auto k_block = [&](KWalk const &w, uint8_t *dA, uint8_t *dB, uint32_t bar) {
-          const int a2 = slot_at(sa, 0, w.ko0, w.ko1), a3 = slot_at(sa, 1, w.ko0, w.ko1),
-                    a4 = slot_at(sa, 2, w.ko0, w.ko1);
-          const int b2 = slot_at(sb, 0, w.ko0, w.ko1), b3 = slot_at(sb, 1, w.ko0, w.ko1),
-                    b4 = slot_at(sb, 2, w.ko0, w.ko1);
+          const int a2 = slot_at(pt.sa, 0, w.ko0, w.ko1), a3 = slot_at(pt.sa, 1, w.ko0, w.ko1),
+                    a4 = slot_at(pt.sa, 2, w.ko0, w.ko1);
+          const int b2 = slot_at(pt.sb, 0, w.ko0, w.ko1), b3 = slot_at(pt.sb, 1, w.ko0, w.ko1),
+                    b4 = slot_at(pt.sb, 2, w.ko0, w.ko1);
           const int kcol = w.kp * BK;
 #pragma unroll
           for (int j = 0; j < (A_MN ? BM / Cfg::kRowsPerBox : 1); ++j) {
-            const int x = A_MN ? mrow + j * Cfg::kRowsPerBox : kcol, y = A_MN ? kcol : mrow;
+            const int x = A_MN ? pt.mrow + j * Cfg::kRowsPerBox : kcol, y = A_MN ? kcol : pt.mrow;
             tma_load_5d_pair(dA + j * BK * 128, &map_a, bar, x, y, a2, a3, a4);
           }
 #pragma unroll
           for (int j = 0; j < (B_MN ? Cfg::kBNh / Cfg::kRowsPerBox : 1); ++j) {
-            const int x = B_MN ? nrow + j * Cfg::kRowsPerBox : kcol, y = B_MN ? kcol : nrow;
+            const int x = B_MN ? pt.nrow + j * Cfg::kRowsPerBox : kcol, y = B_MN ? kcol : pt.nrow;
             tma_load_5d_pair(dB + j * BK * 128, &map_b, bar, x, y, b2, b3, b4);
           }
         };
-        KWalk kw;
-        kw.seek(p, rot * KSUB);
+        KWalk kw = pt.kw;
+        const int rot = pt.rot;
         for (int js = 0; js < n_kstages; ++js) {
           int ksg = js + rot;
           if (ksg >= n_kstages) ksg -= n_kstages;

@@ -19,29 +19,31 @@ __host__ __device__ constexpr uint32_t make_idesc(int kind, int m, int n, bool a
 }
 
 struct TileCoord {
-  int64_t mt, nt;
-  int64_t l[kMaxTileLoops];
+  int mt, nt;
+  int l[kMaxTileLoops];
 };
 
-// tile index -> (M tile, N tile, tile-loop indices); M/N tiles in groups of group_m M tiles
-__device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
+// tile index -> (M tile, N tile, tile-loop indices); M/N tiles in groups of
+// group_m M tiles. 32-bit arithmetic: the planner keeps tile counts below 2^31.
+__device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t tile) {
   TileCoord c;
-  const int64_t mn = (int64_t)p.m_tiles * p.n_tiles;
-  int64_t u = t % mn;
+  uint32_t t = (uint32_t)tile;
+  const uint32_t mn = (uint32_t)p.m_tiles * (uint32_t)p.n_tiles;
+  const uint32_t u = t % mn;
   t /= mn;
-  const int64_t gsz_full = (int64_t)p.group_m * p.n_tiles;
-  const int64_t g = u / gsz_full;
-  const int64_t first_m = g * p.group_m;
-  const int64_t rem_m = p.m_tiles - first_m;
-  const int64_t gm = rem_m < p.group_m ? rem_m : p.group_m;
-  const int64_t r = u - g * gsz_full;
-  c.mt = first_m + r % gm;
-  c.nt = r / gm;
+  const uint32_t gsz_full = (uint32_t)p.group_m * (uint32_t)p.n_tiles;
+  const uint32_t g = u / gsz_full;
+  const uint32_t first_m = g * (uint32_t)p.group_m;
+  const uint32_t rem_m = (uint32_t)p.m_tiles - first_m;
+  const uint32_t gm = rem_m < (uint32_t)p.group_m ? rem_m : (uint32_t)p.group_m;
+  const uint32_t r = u - g * gsz_full;
+  c.mt = (int)(first_m + r % gm);
+  c.nt = (int)(r / gm);
 #pragma unroll
   for (int i = 0; i < kMaxTileLoops; ++i) {
     if (i < p.n_loops) {
-      c.l[i] = t % p.loop_size[i];
-      t /= p.loop_size[i];
+      c.l[i] = (int)(t % (uint32_t)p.loop_size[i]);
+      t /= (uint32_t)p.loop_size[i];
     } else {
       c.l[i] = 0;
     }
@@ -49,14 +51,14 @@ __device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t t) {
   return c;
 }
 
-__device__ __forceinline__ int src_coord(int8_t src, int64_t ko0, int64_t ko1, TileCoord const &c) {
+__device__ __forceinline__ int src_coord(int8_t src, int ko0, int ko1, TileCoord const &c) {
   switch (src) {
-    case kSrcKo0: return (int)ko0;
-    case kSrcKo1: return (int)ko1;
-    case kSrcLoop0: return (int)c.l[0];
-    case kSrcLoop0 + 1: return (int)c.l[1];
-    case kSrcLoop0 + 2: return (int)c.l[2];
-    case kSrcLoop0 + 3: return (int)c.l[3];
+    case kSrcKo0: return ko0;
+    case kSrcKo1: return ko1;
+    case kSrcLoop0: return c.l[0];
+    case kSrcLoop0 + 1: return c.l[1];
+    case kSrcLoop0 + 2: return c.l[2];
+    case kSrcLoop0 + 3: return c.l[3];
     default: return 0;
   }
 }
@@ -117,7 +119,32 @@ struct KWalk {
 // MMA of a tile's walk always initialises the accumulator.
 __device__ __forceinline__ int k_rotation(int64_t t, int n_stages) {
   if (n_stages <= 1) return 0;
-  return (int)((t * 7) % n_stages);
+  return (int)(((uint32_t)t * 7u) % (uint32_t)n_stages);
+}
+
+// Per-tile set-up of the TMA producer: tile coordinates, the operand row
+// origins, the fixed TMA coordinates and the start of the rotated K walk.
+struct ProducerTile {
+  TileCoord c;
+  int rot, mrow, nrow;
+  SlotCoords sa, sb;
+  KWalk kw;
+};
+
+// m_rows / n_cols: output rows / columns of a tile; m_off / n_off: first row
+// of this CTA's operand half within its tile (CTA pairs), else 0
+template <int KSUB>
+__device__ __forceinline__ ProducerTile producer_tile(TcParams const &p, int64_t t, int n_kstages,
+                                                      int m_rows, int m_off, int n_cols, int n_off) {
+  ProducerTile pt;
+  pt.c = decode_tile(p, t);
+  pt.rot = k_rotation(t, n_kstages);
+  pt.mrow = pt.c.mt * m_rows + m_off;
+  pt.nrow = pt.c.nt * n_cols + n_off;
+  pt.sa = slot_coords(p.a_src, pt.c);
+  pt.sb = slot_coords(p.b_src, pt.c);
+  pt.kw.seek(p, pt.rot * KSUB);
+  return pt;
 }
 
 // Epilogue variant of a plan: 0 = ZERO first touch and no last touch, 1 = COPY
