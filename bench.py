@@ -56,7 +56,7 @@ def _peaks():
 
 def _profile_traffic():
     """DRAM bytes per launch of the tensor-core kernel from the committed ncu summary."""
-    f = ROOT / "profiles" / "tc_contract_bf16_cfg2.txt"
+    f = ROOT / "profiles" / "tc_pair_contract_bf16_cfg2.txt"
     if not f.exists():
         return None
     m = re.search(r"dram_bytes_per_launch:\s*([0-9.eE+]+)", f.read_text())
