@@ -237,8 +237,10 @@ __global__ void __launch_bounds__(256)
   }
 }
 
-// transpose mode: dim 0 is the output's stride-1 dim, dim tdim_in the input's
-template <typename T>
+// transpose mode: dim 0 is the output's stride-1 dim, dim tdim_in the input's.
+// I: index type, int32_t whenever every element offset of both tensors fits
+// (the common case; 64-bit divisions in the tile decode cost ~1 us per tile).
+template <typename T, typename I>
 __global__ void __launch_bounds__(256)
     permute_transpose_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
   constexpr int TS = 32;
@@ -247,39 +249,52 @@ __global__ void __launch_bounds__(256)
   const int td = p.tdim_in;
   pdl_launch_dependents();
   pdl_wait();
-  const int64_t s0 = p.size[0], st = p.size[td];
-  const int64_t t0 = (s0 + TS - 1) / TS, tt = (st + TS - 1) / TS;
-  const int64_t nblk = t0 * tt * p.batch;
-  for (int64_t blk = blockIdx.x; blk < nblk; blk += gridDim.x) {
-    int64_t b0 = blk % t0;
-    int64_t r = blk / t0;
-    int64_t bt = r % tt;
-    int64_t bat = r / tt;
-    int64_t oi = 0, oo = 0;
+  const I s0 = (I)p.size[0], st = (I)p.size[td];
+  const I t0 = (s0 + TS - 1) / TS, tt = (st + TS - 1) / TS;
+  const I nblk = t0 * tt * (I)p.batch;
+  const I sin0 = (I)p.sin[0], sint = (I)p.sin[td], sout0 = (I)p.sout[0], soutt = (I)p.sout[td];
+  for (I blk = (I)blockIdx.x; blk < nblk; blk += (I)gridDim.x) {
+    const I b0 = blk % t0;
+    const I r = blk / t0;
+    const I bt = r % tt;
+    I bat = r / tt;
+    I oi = 0, oo = 0;
 #pragma unroll
     for (int d = 1; d < kMaxPermDims; ++d) {
       if (d < p.nd && d != td) {
-        int64_t i = bat % p.size[d];
-        bat /= p.size[d];
-        oi += i * p.sin[d];
-        oo += i * p.sout[d];
+        const I i = bat % (I)p.size[d];
+        bat /= (I)p.size[d];
+        oi += i * (I)p.sin[d];
+        oo += i * (I)p.sout[d];
       }
     }
     // load: consecutive threads walk the input's stride-1 dim
 #pragma unroll
     for (int i = 0; i < TS / 8; ++i) {
-      int64_t it = bt * TS + tx, i0 = b0 * TS + ty + 8 * i;
-      if (it < st && i0 < s0) tile[ty + 8 * i][tx] = in[oi + it * p.sin[td] + i0 * p.sin[0]];
+      const I it = bt * TS + tx, i0 = b0 * TS + ty + 8 * i;
+      if (it < st && i0 < s0) tile[ty + 8 * i][tx] = in[oi + it * sint + i0 * sin0];
     }
     __syncthreads();
     // store: consecutive threads walk the output's stride-1 dim
 #pragma unroll
     for (int i = 0; i < TS / 8; ++i) {
-      int64_t i0 = b0 * TS + tx, it = bt * TS + ty + 8 * i;
-      if (it < st && i0 < s0) out[oo + i0 * p.sout[0] + it * p.sout[td]] = tile[tx][ty + 8 * i];
+      const I i0 = b0 * TS + tx, it = bt * TS + ty + 8 * i;
+      if (it < st && i0 < s0) out[oo + i0 * sout0 + it * soutt] = tile[tx][ty + 8 * i];
     }
     __syncthreads();
   }
+}
+
+// largest element offset of a permute's input or output (non-negative strides)
+static bool offsets_fit_int32(PermuteParams const &p) {
+  int64_t span_in = 0, span_out = 0;
+  for (int d = 0; d < p.nd; ++d) {
+    if (p.sin[d] < 0 || p.sout[d] < 0) return false;
+    span_in += (p.size[d] - 1) * p.sin[d];
+    span_out += (p.size[d] - 1) * p.sout[d];
+  }
+  return span_in < (int64_t(1) << 31) - 1 && span_out < (int64_t(1) << 31) - 1 &&
+         p.total < (int64_t(1) << 31);
 }
 
 template <typename T>
@@ -304,10 +319,15 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
     }
   } else {
     int64_t nblk = ((p.size[0] + 31) / 32) * ((p.size[p.tdim_in] + 31) / 32) * p.batch;
-    int64_t cap = (int64_t)num_sms * 8;
+    int64_t cap = (int64_t)num_sms * 8;  // 8 x 256 threads fill an SM: the copy is latency bound
     int64_t blocks = nblk < cap ? nblk : cap;
     if (blocks < 1) blocks = 1;
-    e = launch_kernel(permute_transpose_kernel<T>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    if (offsets_fit_int32(p))
+      e = launch_kernel(permute_transpose_kernel<T, int32_t>, dim3((unsigned)blocks), dim3(256), 0, st,
+                        p, i, o);
+    else
+      e = launch_kernel(permute_transpose_kernel<T, int64_t>, dim3((unsigned)blocks), dim3(256), 0, st,
+                        p, i, o);
   }
   return e;
 }
