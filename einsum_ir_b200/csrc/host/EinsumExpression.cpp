@@ -136,6 +136,7 @@ err_t EinsumExpression::compile() {
   }
   for (auto &n : m_nodes) n.m_compute = m_compute;
   err_t err = m_nodes.back().compile();
+  if (m_stream != nullptr) m_nodes.back().set_stream(m_stream);
   m_compiled = true;
   return err;
 }
@@ -160,6 +161,7 @@ int EinsumExpression::eval() {
 int64_t EinsumExpression::num_ops() { return m_nodes.empty() ? 0 : m_nodes.back().num_ops(true); }
 
 void EinsumExpression::set_stream(void *i_stream) {
+  m_stream = i_stream;  // applied to the nodes now and at every compile
   if (!m_nodes.empty()) m_nodes.back().set_stream(i_stream);
 }
 

@@ -65,6 +65,7 @@ class EinsumExpression {
   data_t m_dtype = UNDEFINED_DTYPE;
   data_t m_dtype_inputs = UNDEFINED_DTYPE;
   int32_t m_compute = 0;
+  void *m_stream = nullptr;
   void *const *m_data_ptrs = nullptr;
   std::vector<int64_t> m_path_int;
   std::map<int64_t, int64_t> m_map_dim_sizes;

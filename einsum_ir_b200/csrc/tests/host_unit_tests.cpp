@@ -5,6 +5,7 @@
 //   BinaryPrimitives.test.cpp:4-62      swap_inputs
 //   EinsumExpressionAscii.test.cpp      parsers
 //   MemoryManager.test.cpp:5            two-ended arena (same tree, current API names)
+//   EinsumTree.test.torch.cpp:9-164     tree strings (the trees of its three cases)
 #include <cstdio>
 #include <iostream>
 #include <map>
@@ -13,6 +14,7 @@
 #include "BinaryContraction.h"
 #include "BinaryPrimitives.h"
 #include "EinsumExpression.h"
+#include "EinsumTree.h"
 #include "MemoryManager.h"
 
 using namespace einsum_ir;
@@ -21,6 +23,7 @@ using backend::BinaryPrimitives;
 using backend::MemoryManager;
 using frontend::EinsumExpression;
 using frontend::EinsumExpressionAscii;
+using frontend::EinsumTreeAscii;
 
 static int g_fail = 0, g_checks = 0;
 #define CHECK(cond)                                                   \
@@ -164,6 +167,34 @@ static void test_memory_manager() {
   CHECK(mm.m_req_mem >= (30 + 30 + 15) * 4);
 }
 
+static void test_tree_ascii() {
+  using V = std::vector<int64_t>;
+  std::string t = "[[3,0]->[0,3]],[[3,2,4],[1,4,2]->[1,2,3]]->[0,1,2]";
+  int64_t n = EinsumTreeAscii::count_nodes(t);
+  CHECK(n == 6);
+  std::vector<V> ids(n), ch(n);
+  int64_t next = 0;
+  CHECK(EinsumTreeAscii::parse_tree(t, ids, ch, next) == SUCCESS && next == 6);
+  std::vector<V> eids = {{3, 0}, {0, 3}, {3, 2, 4}, {1, 4, 2}, {1, 2, 3}, {0, 1, 2}};
+  std::vector<V> ech = {{}, {0}, {}, {}, {2, 3}, {1, 4}};
+  CHECK(ids == eids && ch == ech);
+  std::map<int64_t, int64_t> sz;
+  EinsumTreeAscii::parse_dim_size("2,3,4,5,6", ids, sz);
+  CHECK(sz.size() == 5 && sz[0] == 2 && sz[1] == 3 && sz[2] == 4 && sz[3] == 5 && sz[4] == 6);
+  CHECK(EinsumTreeAscii::count_nodes("[0,3],[1,2,3]->[0,1,2]") == 3);
+  CHECK(EinsumTreeAscii::count_nodes("[0,1]->[1,0]") == 2);
+  std::vector<V> i2(2), c2(2);
+  next = 0;
+  CHECK(EinsumTreeAscii::parse_tree("[0,1]->[1,0]", i2, c2, next) == SUCCESS && next == 2);
+  CHECK(i2[1] == (V{1, 0}) && c2[1] == (V{0}));
+  std::string l, r, o;
+  CHECK(EinsumTreeAscii::split_outer_operation("[0,3],[1,2,3]->[0,1,2]", l, r, o) == SUCCESS);
+  CHECK(l == "0,3" && r == "1,2,3" && o == "0,1,2");
+  std::vector<V> bad(2), badc(2);
+  next = 0;
+  CHECK(EinsumTreeAscii::parse_tree("[0,1]>[1,0]", bad, badc, next) != SUCCESS);
+}
+
 // --cases: read one case per line from stdin and print this backend's answer
 // (used by the test suite to compare against the reference's own functions):
 //   T nl nr no <ids...>   -> dim types of left, right, out
@@ -171,6 +202,7 @@ static void test_memory_manager() {
 //   U n <path...>         -> unique_tensor_ids
 //   B nl nr nh <ids...> <hist...> -> substring_out
 //   D <expression>        -> parse_dim_ids as name:id;...
+//   E <tree> <sizes>      -> tree nodes as "ids:children;" ... "|id=size," (or -1)
 static int run_cases() {
   std::string tag;
   while (std::cin >> tag) {
@@ -217,6 +249,26 @@ static int run_cases() {
       EinsumExpressionAscii::parse_dim_ids(e, ids);
       for (auto const &kv : ids) std::cout << kv.first << ":" << kv.second << ";";
       std::cout << "\n";
+    } else if (tag == "E") {
+      std::string t, sizes;
+      std::cin >> t >> sizes;
+      int64_t n = EinsumTreeAscii::count_nodes(t), next = 0;
+      std::vector<std::vector<int64_t>> ids(n), ch(n);
+      if (EinsumTreeAscii::parse_tree(t, ids, ch, next) != SUCCESS || next != n) {
+        std::cout << "-1\n";
+      } else {
+        std::map<int64_t, int64_t> sz;
+        EinsumTreeAscii::parse_dim_size(sizes, ids, sz);
+        for (int64_t i = 0; i < n; ++i) {
+          for (auto x : ids[i]) std::cout << x << ",";
+          std::cout << ":";
+          for (auto x : ch[i]) std::cout << x << ",";
+          std::cout << ";";
+        }
+        std::cout << "|";
+        for (auto const &kv : sz) std::cout << kv.first << "=" << kv.second << ",";
+        std::cout << "\n";
+      }
     }
     std::cout.flush();
   }
@@ -230,6 +282,7 @@ int main(int argc, char **argv) {
   test_swap_inputs();
   test_reorder_policy();
   test_ascii();
+  test_tree_ascii();
   test_memory_manager();
   std::printf("%d checks, %d failed\n", g_checks, g_fail);
   return g_fail == 0 ? 0 : 1;

@@ -7,7 +7,7 @@ HERE := $(dir $(abspath $(lastword $(MAKEFILE_LIST))))
 OUT := $(HERE)_ref
 SRCS := $(REF)/src/backend/BinaryContraction.cpp $(REF)/src/backend/BinaryPrimitives.cpp \
         $(REF)/src/frontend/EinsumExpression.cpp $(REF)/src/frontend/EinsumExpressionAscii.cpp \
-        $(HERE)ref_wrap.cpp
+        $(REF)/src/frontend/EinsumTreeAscii.cpp $(HERE)ref_wrap.cpp
 CXXFLAGS := -O1 -std=c++17 -fPIC -ffunction-sections -fdata-sections -fopenmp -w -I$(REF)/src
 
 all: $(OUT)/libref_struct.so

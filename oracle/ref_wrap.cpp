@@ -11,11 +11,13 @@
 #include "backend/BinaryPrimitives.h"
 #include "frontend/EinsumExpression.h"
 #include "frontend/EinsumExpressionAscii.h"
+#include "frontend/EinsumTreeAscii.h"
 
 using einsum_ir::backend::BinaryContraction;
 using einsum_ir::backend::BinaryPrimitives;
 using einsum_ir::frontend::EinsumExpression;
 using einsum_ir::frontend::EinsumExpressionAscii;
+using einsum_ir::frontend::EinsumTreeAscii;
 
 extern "C" {
 
@@ -66,6 +68,29 @@ int64_t ref_parse_dim_ids(const char *expr, char *out, int64_t cap) {
 int64_t ref_schar_to_standard(const char *expr, char *out, int64_t cap) {
   std::string s;
   EinsumExpressionAscii::schar_to_standard(expr, s);
+  std::strncpy(out, s.c_str(), (size_t)cap);
+  return (int64_t)s.size();
+}
+
+// einsum tree string -> "ids:children;" per node (post order) then "|id=size,"
+// for the dimension sizes; returns -1 if the reference parser rejects the tree
+int64_t ref_parse_tree(const char *tree, const char *sizes, char *out, int64_t cap) {
+  std::string t(tree);
+  int64_t n = EinsumTreeAscii::count_nodes(t);
+  std::vector<std::vector<int64_t>> ids(n), ch(n);
+  int64_t next = 0;
+  if (EinsumTreeAscii::parse_tree(t, ids, ch, next) != einsum_ir::SUCCESS || next != n) return -1;
+  std::map<int64_t, int64_t> sz;
+  EinsumTreeAscii::parse_dim_size(sizes, ids, sz);
+  std::string s;
+  for (int64_t i = 0; i < n; ++i) {
+    for (auto x : ids[i]) s += std::to_string(x) + ",";
+    s += ":";
+    for (auto x : ch[i]) s += std::to_string(x) + ",";
+    s += ";";
+  }
+  s += "|";
+  for (auto const &kv : sz) s += std::to_string(kv.first) + "=" + std::to_string(kv.second) + ",";
   std::strncpy(out, s.c_str(), (size_t)cap);
   return (int64_t)s.size();
 }

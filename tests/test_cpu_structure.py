@@ -127,6 +127,41 @@ def test_parse_dim_ids_match_reference():
         assert buf.value.decode() == h
 
 
+def _random_tree(rng, depth=0):
+    """A random einsum tree string (leaves, permutes, binary nodes) and its root dims."""
+    r = rng.random()
+    if depth >= 3 or r < 0.3:
+        ids = rng.sample(range(14), rng.randint(1, 4))
+        return ",".join(map(str, ids)), ids
+    if r < 0.45:
+        s, ids = _random_tree(rng, depth + 1)
+        out = ids[:]
+        rng.shuffle(out)
+        return f"[{s}]->[{','.join(map(str, out))}]", out
+    (sl, il), (sr, ir) = _random_tree(rng, depth + 1), _random_tree(rng, depth + 1)
+    both = list(dict.fromkeys(il + ir))
+    out = [d for d in both if rng.random() < 0.7] or both[:1]
+    rng.shuffle(out)
+    return f"[{sl}],[{sr}]->[{','.join(map(str, out))}]", out
+
+
+def test_tree_parser_matches_reference():
+    L = _ref()
+    rng = random.Random(3)
+    trees = ["[[3,0]->[0,3]],[[3,2,4],[1,4,2]->[1,2,3]]->[0,1,2]", "[0,3],[1,2,3]->[0,1,2]",
+             "[0,1]->[1,0]"] + [_random_tree(rng)[0] for _ in range(150)]
+    trees = [t for t in trees if t.startswith("[")]
+    lines = []
+    for t in trees:
+        n_ids = len(set(int(x) for x in re.findall(r"\d+", t)))
+        lines.append((t, ",".join(str(2 + i) for i in range(n_ids))))
+    host = _host([f"E {t} {sz}" for t, sz in lines])
+    for (t, sz), h in zip(lines, host):
+        buf = ctypes.create_string_buffer(1 << 16)
+        k = L.ref_parse_tree(t.encode(), sz.encode(), buf, 1 << 16)
+        assert (buf.value.decode() if k >= 0 else "-1") == h, t
+
+
 PLAN_CASES = [
     # expression, sizes, dtype, compute, expected lowering fragments
     ("akmj,njk->anm", dict(a=16, k=32, m=512, j=64, n=512), cabi.BF16, 0,

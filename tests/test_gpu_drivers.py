@@ -21,7 +21,7 @@ def _run(args, timeout=300):
 
 
 def test_drivers_print_usage_without_arguments():
-    for exe in ("bench_expression", "bench_binary"):
+    for exe in ("bench_expression", "bench_binary", "bench_tree"):
         r = _run([PKG / exe])
         assert r.returncode != 0
         assert "Usage:" in r.stderr
@@ -60,4 +60,32 @@ def test_bench_binary(cuda, expr, sizes, dtype):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     assert "results are close" in r.stdout
     rel = float(re.search(r"relative error vs FP64 CUDA-core solution: (\S+)", r.stdout).group(1))
+    assert rel <= TOL[dtype]
+
+
+TREES = [
+    # the reference's EinsumTree test trees (EinsumTree.test.torch.cpp:9-164)
+    ("[0,3],[1,2,3]->[0,1,2]", "2,4,6,8", "FP32"),
+    ("[0,1]->[1,0]", "7,3", "FP32"),
+    ("[[3,0]->[0,3]],[[3,2,4],[1,4,2]->[1,2,3]]->[0,1,2]", "2,3,4,5,6", "FP64"),
+    # a ring of four 3-way tensors contracted pairwise (tensor-core sized root)
+    ("[[0,1,2],[2,3,4]->[0,1,3,4]],[[4,5,6],[6,7,0]->[4,5,7,0]]->[1,3,5,7]",
+     "32,32,32,32,32,32,32,32", "FP32"),
+    ("[[0,1,2],[2,3,4]->[0,1,3,4]],[[4,5,6],[6,7,0]->[4,5,7,0]]->[1,3,5,7]",
+     "32,32,32,32,32,32,32,32", "BF16"),
+    ("[[0,1,2],[2,3,4]->[0,1,3,4]],[[4,5,6],[6,7,0]->[4,5,7,0]]->[1,3,5,7]",
+     "32,32,32,32,32,32,32,32", "TF32"),
+    ("[[0,1,2],[2,3,4]->[0,1,3,4]],[[4,5,6],[6,7,0]->[4,5,7,0]]->[1,3,5,7]",
+     "16,16,16,16,16,16,16,16", "FP64"),
+    # a permute at the root
+    ("[[0,1],[1,2]->[0,2]]->[2,0]", "256,256,256", "FP32"),
+]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("tree,sizes,dtype", TREES)
+def test_bench_tree(cuda, tree, sizes, dtype):
+    r = _run([PKG / "bench_tree", tree, sizes, dtype])
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    rel = float(re.search(r"relative error:\s+(\S+)", r.stdout).group(1))
     assert rel <= TOL[dtype]
