@@ -437,7 +437,7 @@ bool try_tc(eir_plan *p, std::string *why) {
 
   const int bk = eir::tc_block_k(kind);
   // Tile shape. One CTA per 128 x BN tile stages 128 + BN operand rows per K
-  // block; a CTA pair (256 x BN over two SMs, kinds BF16 / TF32) stages
+  // block; a CTA pair (256 x BN over two SMs, kinds BF16 / TF32 / 3xTF32) stages
   // 128 + BN/2 rows per SM for the same 128 x BN outputs per SM. Operand rows
   // staged per SM (the L2 -> SM traffic) set the time of a tile once K is
   // long; minimise waves x (rows per SM + a fixed per-tile overhead).
@@ -448,7 +448,7 @@ bool try_tc(eir_plan *p, std::string *why) {
   if (device_state(&ds) == EIR_SUCCESS) num_sms = ds->num_sms;
   int bn = 128;
   bool pair = false;
-  if (kind != 2 && kind != 3) {
+  if (kind != 3) {
     const int64_t force_bn = env_int("EIR_TC_BN", 0);     // tuning override: 128 or 256
     const int64_t force_pair = env_int("EIR_TC_PAIR", -1);  // tuning override: 0 or 1
     double best = 0.0;
@@ -457,6 +457,7 @@ bool try_tc(eir_plan *p, std::string *why) {
       if (force_pair == 1 && pr == 0 && d[mp].size > 128) continue;
       if (pr == 1 && d[mp].size <= 128) continue;  // a pair tile would be half empty
       for (int cbn : {128, 256}) {
+        if (kind == 2 && pr == 0 && cbn == 256) continue;  // one-CTA 3xTF32: BN = 128 only
         if ((force_bn == 128 || force_bn == 256) && cbn != force_bn) continue;
         if (cbn == 256 && d[np].size <= 128 && force_bn != 256) continue;
         const int64_t tiles = ceil_div(d[mp].size, pr ? 256 : 128) * ceil_div(d[np].size, cbn) *

@@ -20,7 +20,8 @@ cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
                                float const *aux, float *out, int num_sms, cudaStream_t st);
 
 // CTA pairs (cta_group::2): 256 x BN tiles, each CTA stages half of A's and
-// half of B's rows; kind 0 or 1, bn 128 or 256, ksub 1 or 2
+// half of B's rows; kind 0 or 1 (bn 128 or 256, ksub 1 or 2) or 2 (3xTF32,
+// bn 128 or 256, ksub 1)
 cudaError_t launch_tc_pair_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
                                     CUtensorMap const &ma, CUtensorMap const &mb, TcParams const &p,
                                     float const *aux, float *out, cudaStream_t st);

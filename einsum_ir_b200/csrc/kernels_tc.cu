@@ -18,9 +18,10 @@
 // Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+TMEM owner),
 // warps 2..5 = epilogue (TMEM -> registers -> global, fused first/last touch:
 // ZERO/COPY/ADD before, RELU/ADD after, aux read through broadcast strides),
-// warps 6..9 (3xTF32 only) = split each staged FP32 tile into hi + lo TF32
-// parts in shared memory (hi = round-to-nearest TF32, lo = x - hi) so three
-// MMAs (lo*hi + hi*lo + hi*hi) give an FP32-accurate product.
+// warps 6..9 (3xTF32 only) = store lo = x - trunc_TF32(x) of each staged FP32
+// tile next to it in shared memory (the staged x is the hi part, see
+// split_tf32_lo) so three MMAs (lo*hi + hi*lo + hi*hi) give an FP32-accurate
+// product.
 //
 // Semantics follow the reference loop engine: first touch at the first K
 // step, last touch after the last (ContractionBackend.cpp:296-348,495-515;
@@ -56,22 +57,6 @@ struct TcConfig {
   static_assert(kTmemCols == 256 || kTmemCols == 512, "TMEM allocation must be a power of two");
   static_assert(kSmemBytes <= 232448, "shared memory budget");
 };
-
-__device__ __forceinline__ uint32_t cvt_rna_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return r;
-}
-
-__device__ __forceinline__ void split_tf32(float4 *hi_io, float4 *lo_out) {
-  float4 x = *hi_io, h, l;
-  h.x = __uint_as_float(cvt_rna_tf32(x.x)); l.x = x.x - h.x;
-  h.y = __uint_as_float(cvt_rna_tf32(x.y)); l.y = x.y - h.y;
-  h.z = __uint_as_float(cvt_rna_tf32(x.z)); l.z = x.z - h.z;
-  h.w = __uint_as_float(cvt_rna_tf32(x.w)); l.w = x.w - h.w;
-  *hi_io = h;
-  *lo_out = l;
-}
 
 template <int KIND, int BN, int KSUB, bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
@@ -316,11 +301,11 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
         float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32(&a[i], &alo[i]);
+        for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32_lo(&a[i], &alo[i]);
         float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
         float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32(&b[i], &blo[i]);
+        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32_lo(&b[i], &blo[i]);
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
         if (++stage == S) {

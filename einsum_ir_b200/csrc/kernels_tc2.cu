@@ -18,7 +18,10 @@
 // Warp roles per CTA: warp 0 = TMA producer, warp 1 = MMA issuer (leader) and
 // TMEM owner (both CTAs allocate with cta_group::2), warps 2..9 = epilogue, two
 // per TMEM lane quadrant with half of the columns each (fused first / last
-// touch as in the one-CTA kernel). Every wait is bounded;
+// touch as in the one-CTA kernel). FP32-exact mode (3xTF32): warps 2..5 =
+// epilogue, warps 6..9 split each CTA's staged FP32 tiles into hi / lo TF32
+// parts; the loads of a CTA then complete on its own barrier and the MMA
+// issuer waits for the converter warps of both CTAs. Every wait is bounded;
 // a timeout raises the abort flag in both CTAs and records a device error.
 #include <cuda.h>
 #include "eir_common.cuh"
@@ -41,12 +44,17 @@ struct PairConfig {
   static constexpr int kBSub = kBNh * 128;
   static constexpr int kABytes = KSUB * kASub;
   static constexpr int kBBytes = KSUB * kBSub;
-  static constexpr int kStageBytes = kABytes + kBBytes;
+  // FP32-exact mode keeps a hi and a lo TF32 copy of every staged operand
+  static constexpr bool kSplit = (KIND == kKind3xTF32);
+  static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
   static constexpr int kMaxStages = 8;
   static constexpr int kFit = (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
-  static constexpr int kEpiWarps = 8;             // 2 per TMEM lane quadrant, half the columns each
-  static constexpr int kThreads = 32 * (2 + kEpiWarps);
+  // epilogue: 2 warps per TMEM lane quadrant (half the columns each), or 1 in
+  // FP32-exact mode, whose 4 converter warps split the staged tiles
+  static constexpr int kEpiWarps = kSplit ? 4 : 8;
+  static constexpr int kConvWarps = kSplit ? 4 : 0;
+  static constexpr int kThreads = 32 * (2 + kEpiWarps + kConvWarps);
   static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
   static_assert(kStages >= 2, "at least two ring stages");
@@ -70,13 +78,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t *sA = smem;                   // S x kABytes
   uint8_t *sB = sA + S * Cfg::kABytes;  // S x kBBytes
+  uint8_t *sAlo = sB + S * Cfg::kBBytes;                       // (split) S x kABytes
+  uint8_t *sBlo = sAlo + (Cfg::kSplit ? S * Cfg::kABytes : 0);  // (split) S x kBBytes
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
-  uint64_t *full = bars;                // S (leader's count both CTAs' bytes)
+  uint64_t *full = bars;                // S (leader's count both CTAs' bytes; split: own bytes)
   uint64_t *empty = bars + S;           // S
   uint64_t *tfull = bars + 2 * S;       // 2
   uint64_t *tempty = bars + 2 * S + 2;  // 2 (leader's: epilogue warps of both CTAs)
   uint64_t *drain = bars + 2 * S + 4;   // 1 (leader: all MMAs done)
-  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 2 * S + 5);
+  uint64_t *conv = bars + 2 * S + 5;    // S (split, leader's: converter warps of both CTAs)
+  uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
   const int warp = threadIdx.x >> 5;
@@ -97,6 +108,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       mbar_init(&tempty[a], 2 * Cfg::kEpiWarps);
     }
     mbar_init(drain, 1);
+    for (int s = 0; s < S; ++s) mbar_init(&conv[s], 2 * Cfg::kConvWarps);
     *abort_flag = 0;
     fence_barrier_init();
   }
@@ -164,8 +176,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
             break;
           }
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
-          if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (Cfg::kASub + Cfg::kBSub));
-          const uint32_t bar = full_leader + 8u * (uint32_t)stage;
+          // FP32-exact mode: each CTA's loads complete on its own barrier (its
+          // converter warps wait there); otherwise on the leader's, for both
+          if (Cfg::kSplit) mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
+          else if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (Cfg::kASub + Cfg::kBSub));
+          const uint32_t bar = Cfg::kSplit ? smem_u32(&full[stage]) : full_leader + 8u * (uint32_t)stage;
           for (int sub = 0; sub < nsub; ++sub, kw.next(p))
             k_block(kw, sA + stage * Cfg::kABytes + sub * Cfg::kASub,
                     sB + stage * Cfg::kBBytes + sub * Cfg::kBSub, bar);
@@ -218,7 +233,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
           int ksg = js + rot;
           if (ksg >= n_kstages) ksg -= n_kstages;
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
-          if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
+          if (!mbar_wait_bounded(Cfg::kSplit ? &conv[stage] : &full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
@@ -235,8 +250,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
                 const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
                 const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
                 const uint32_t accum = (js > 0 || sub > 0 || kk > 0) ? 1u : 0u;
-                if (KIND == kKindBF16) umma_f16_pair(d_tmem, adesc, bdesc, idesc, accum);
-                else umma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
+                if (KIND == kKindBF16) {
+                  umma_f16_pair(d_tmem, adesc, bdesc, idesc, accum);
+                } else if (KIND == kKindTF32) {
+                  umma_tf32_pair(d_tmem, adesc, bdesc, idesc, accum);
+                } else {
+                  const uint32_t alo_base = smem_u32(sAlo + stage * Cfg::kABytes + sub * Cfg::kASub);
+                  const uint32_t blo_base = smem_u32(sBlo + stage * Cfg::kBBytes + sub * Cfg::kBSub);
+                  const uint64_t alo = make_smem_desc(alo_base + a_off, a_lbo, a_sbo, a_lay);
+                  const uint64_t blo = make_smem_desc(blo_base + b_off, b_lbo, b_sbo, b_lay);
+                  umma_tf32_pair(d_tmem, alo, bdesc, idesc, accum);  // small terms first
+                  umma_tf32_pair(d_tmem, adesc, blo, idesc, 1u);
+                  umma_tf32_pair(d_tmem, adesc, bdesc, idesc, 1u);
+                }
               }
             }
           }
@@ -258,7 +284,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       if (!mbar_wait_bounded(drain, 0u, abort_flag) && !*abort_flag) ok = false;
       if (!ok) raise_abort(kErrTimeoutMma);
     }
-  } else {
+  } else if (warp < 2 + Cfg::kEpiWarps) {
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int q = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = q * 32 + lane;
@@ -300,6 +326,40 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
     }
+  } else if (Cfg::kSplit) {
+    // ------------------------------------------------------------ hi/lo split (both CTAs)
+    // each CTA splits its own staged halves, then every converter warp of the
+    // pair arrives on the leader's conv barrier, which the MMA issuer waits on
+    const int ct = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);  // 0 .. 32 * kConvWarps - 1
+    constexpr int kCt = 32 * Cfg::kConvWarps;
+    const uint32_t conv_leader = mapa_shared(smem_u32(conv), 0);
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true;
+    for (int64_t t = pair_id; t < p.total_tiles && ok; t += n_pairs) {
+      for (int js = 0; js < n_kstages; ++js) {
+        if (!mbar_wait_warp(&full[stage], phase, abort_flag)) {
+          ok = false;
+          break;
+        }
+        float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
+        float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
+#pragma unroll 4
+        for (int i = ct; i < Cfg::kABytes / 16; i += kCt) split_tf32_lo(&a[i], &alo[i]);
+        float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
+        float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+#pragma unroll 4
+        for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) split_tf32_lo(&b[i], &blo[i]);
+        fence_proxy_async_smem();  // the tensor cores read these tiles
+        __syncwarp();
+        if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(conv_leader + 8u * (uint32_t)stage);
+        if (++stage == S) {
+          stage = 0;
+          phase ^= 1u;
+        }
+      }
+    }
+    if (!ok && (threadIdx.x & 31) == 0) raise_abort(kErrTimeoutConvert);
   }
 
   // After an abort, copies or commits issued before it may still be landing in
@@ -374,6 +434,10 @@ cudaError_t launch_tc_pair_contract(int kind, int bn, int ksub, bool a_mn, bool 
     return launch_pair_major<kKindTF32, 128, 2>(a_mn, b_mn, ma, mb, p, aux, out, st);
   if (kind == kKindTF32 && bn == 128 && ksub == 1)
     return launch_pair_major<kKindTF32, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKind3xTF32 && bn == 256 && ksub == 1)
+    return launch_pair_major<kKind3xTF32, 256, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
+  if (kind == kKind3xTF32 && bn == 128 && ksub == 1)
+    return launch_pair_major<kKind3xTF32, 128, 1>(a_mn, b_mn, ma, mb, p, aux, out, st);
   return cudaErrorInvalidValue;
 }
 

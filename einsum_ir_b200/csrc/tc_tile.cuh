@@ -147,6 +147,18 @@ __device__ __forceinline__ ProducerTile producer_tile(TcParams const &p, int64_t
   return pt;
 }
 
+// FP32-exact mode (3xTF32): x = hi + lo with hi = x truncated to TF32 and
+// lo = x - hi (exact in FP32); three TF32 MMAs lo*hi + hi*lo + hi*hi give an
+// FP32-accurate product (the error-compensated TF32 method). The tensor core
+// reads a TF32 operand from an FP32 word by ignoring its 13 low mantissa bits,
+// so the staged x already is hi: only lo has to be computed and stored. The
+// FP32 parity tests (relative error ~1e-6 against the oracle) pin this.
+__device__ __forceinline__ void split_tf32_lo(float4 const *x_in, float4 *lo_out) {
+  const float4 x = *x_in;
+  auto lo = [](float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); };
+  *lo_out = make_float4(lo(x.x), lo(x.y), lo(x.z), lo(x.w));
+}
+
 // Epilogue variant of a plan: 0 = ZERO first touch and no last touch, 1 = COPY
 // (bias) first touch with no last touch or RELU, 2 = anything else.
 __device__ __forceinline__ int epilogue_kind(TcParams const &p) {

@@ -135,9 +135,9 @@ def _m_size(expr, sizes):
 
 
 @pytest.mark.parametrize("pair", [0, 1])
-@pytest.mark.parametrize("expr,sizes,dtype", [c for c in TC_CASES if c[2] != "fp32"])
+@pytest.mark.parametrize("expr,sizes,dtype", TC_CASES)
 def test_tc_parity_tile_shapes(cuda, expr, sizes, dtype, pair):
-    """Every BF16 / TF32 case on the one-CTA kernel and on CTA pairs (cta_group::2)."""
+    """Every tensor-core case on the one-CTA kernel and on CTA pairs (cta_group::2)."""
     plan, _ = run_case(cuda, expr, sizes, dtype, expect_family=TC, pair=pair)
     assert ("pair" in plan.describe()) == (pair == 1 and _m_size(expr, sizes) > 128), plan.describe()
 
@@ -149,9 +149,14 @@ PAIR_CASES = [
     ("km,kn->nm", dict(m=384, n=136, k=72), "bf16", 128, 2),
     ("km,kn->nm", dict(m=260, n=520, k=40), "tf32", 256, 1),
     ("mk,kn->nm", dict(m=512, n=256, k=256), "tf32", 128, 1),
+    # FP32-exact (3xTF32) on pairs: hi / lo split by each CTA's converter warps
+    ("mk,nk->nm", dict(m=300, n=200, k=96), "fp32", 256, 1),
+    ("km,kn->nm", dict(m=384, n=136, k=72), "fp32", 128, 1),
+    ("zcdef,zabcd->zabef", dict(z=3, a=16, b=8, c=8, d=8, e=16, f=16), "fp32", 256, 1),
     # several tiles per pair (persistent loop, accumulator double buffering)
     ("cmk,cnk->cnm", dict(c=40, m=512, n=512, k=128), "bf16", 256, 2),
     ("akmj,njk->anm", dict(a=4, k=8, m=512, j=64, n=512), "bf16", 256, 2),
+    ("cmk,cnk->cnm", dict(c=12, m=512, n=512, k=64), "fp32", 256, 1),
 ]
 
 
