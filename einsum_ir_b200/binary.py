@@ -80,8 +80,9 @@ def swap_inputs(ids_left, ids_right, ids_out) -> bool:
 
 def contraction_dims(ids_left, ids_right, ids_out, sizes_inner: Mapping[int, int],
                      sizes_outer_left=None, sizes_outer_right=None, sizes_outer_out=None,
-                     sizes_outer_aux=None) -> List[tuple]:
-    """eir_dim tuples (type, size, stride_left, stride_right, stride_out, stride_aux)."""
+                     sizes_outer_aux=None, cpx_id=None) -> List[tuple]:
+    """eir_dim tuples (type, size, stride_left, stride_right, stride_out, stride_aux).
+    cpx_id: id of the complex dim (size 2, in all three tensors) -> type DIM_CPX."""
     sl = strides(ids_left, sizes_outer_left or sizes_inner)
     sr = strides(ids_right, sizes_outer_right or sizes_inner)
     so = strides(ids_out, sizes_outer_out or sizes_inner)
@@ -92,7 +93,8 @@ def contraction_dims(ids_left, ids_right, ids_out, sizes_inner: Mapping[int, int
     dims = []
     for t, key in ((C, "c"), (M, "m"), (N, "n"), (K, "k")):
         for d in g[key]:
-            dims.append((t, int(sizes_inner[d]), sl.get(d, 0), sr.get(d, 0),
+            ty = cabi.DIM_CPX if d == cpx_id else t
+            dims.append((ty, int(sizes_inner[d]), sl.get(d, 0), sr.get(d, 0),
                          so.get(d, 0) if t != K else 0, sa.get(d, 0) if t != K else 0))
     return dims
 

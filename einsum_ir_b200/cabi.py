@@ -16,10 +16,11 @@ LIB_PATH = PKG / "libeinsum_ir_b200.so"
 
 # ---- enums (values of include/eir_cuda.h)
 SUCCESS = 0
-DIM_C, DIM_M, DIM_N, DIM_K = 0, 1, 2, 3
+DIM_C, DIM_M, DIM_N, DIM_K, DIM_CPX = 0, 1, 2, 3, 4
 FP32, FP64, BF16 = 0, 1, 2
 COMPUTE_DEFAULT, COMPUTE_FP32, COMPUTE_TF32, COMPUTE_FP64, COMPUTE_BF16 = 0, 1, 2, 3, 4
 KTYPE_ZERO, KTYPE_RELU, KTYPE_ADD, KTYPE_COPY, KTYPE_MADD, KTYPE_UNDEFINED = 0, 1, 2, 3, 4, 99
+KTYPE_CPX_ZERO, KTYPE_CPX_MADD = 6, 8
 FAMILY_NONE, FAMILY_SIMT, FAMILY_TC, FAMILY_PERMUTE, FAMILY_DMMA = 0, 1, 2, 3, 4
 FLAG_FORCE_SIMT, FLAG_NO_PREPACK = 1, 2
 

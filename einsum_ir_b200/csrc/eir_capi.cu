@@ -703,12 +703,110 @@ char const *eir_last_error_string(void) { return g_last_error.c_str(); }
 
 int64_t eir_launch_count(void) { return g_launches.load(); }
 
+// Complex contraction (one EIR_DIM_CPX dim of size 2 in left, right and out,
+// CPX_MADD main kernel; reference: BinaryContraction.cpp:453-462 for num_ops,
+// ContractionBackend.cpp:663-675 for the complex strides). Lowered to one real
+// contraction: out[co] = sum_ci A[ci] * B'[ci][co] with B' = [[Br, Bi], [-Bi, Br]],
+// i.e. the complex dim becomes a K dim of A (ci) and an N dim of out (co),
+// and B' is the right operand expanded into four packed real blocks.
+static int create_complex_plan(eir_contract_desc const *desc, eir_plan **plan_out) {
+  int cpx = -1;
+  for (int i = 0; i < desc->num_dims; ++i) {
+    if (desc->dims[i].type != EIR_DIM_CPX) continue;
+    if (cpx >= 0) return set_error(EIR_INVALID_CPX_DIM, "more than one complex dim");
+    cpx = i;
+  }
+  eir_dim const &x = desc->dims[cpx];
+  if (x.size != 2) return set_error(EIR_INVALID_CPX_DIM, "the complex dim must have size 2");
+  if (desc->ktype_main != EIR_KTYPE_CPX_MADD ||
+      (desc->ktype_first_touch != EIR_KTYPE_CPX_ZERO && desc->ktype_first_touch != EIR_KTYPE_UNDEFINED) ||
+      desc->ktype_last_touch != EIR_KTYPE_UNDEFINED)
+    return set_error(EIR_INVALID_KTYPE, "complex contractions take CPX_ZERO / CPX_MADD only");
+  const int dt = desc->dtype_left;
+  if (dt != desc->dtype_right || dt != desc->dtype_out || (dt != EIR_FP32 && dt != EIR_FP64))
+    return set_error(EIR_INVALID_DTYPE, "complex contractions: FP32 or FP64 throughout");
+  // B's other dims, packed with the smallest right stride innermost
+  std::vector<int> bdims;
+  for (int i = 0; i < desc->num_dims; ++i) {
+    int t = desc->dims[i].type;
+    if (i != cpx && (t == EIR_DIM_C || t == EIR_DIM_N || t == EIR_DIM_K)) bdims.push_back(i);
+  }
+  if ((int)bdims.size() > eir::kMaxPermDims)
+    return set_error(EIR_COMPILATION_FAILED, "too many dims in the right operand");
+  std::stable_sort(bdims.begin(), bdims.end(), [&](int a, int b) {
+    return std::llabs(desc->dims[a].stride_right) < std::llabs(desc->dims[b].stride_right);
+  });
+  std::vector<int64_t> packed(desc->num_dims, 0);
+  int64_t nb = 1;
+  for (int i : bdims) {
+    packed[i] = nb;
+    nb *= desc->dims[i].size;
+  }
+  // the real problem
+  std::vector<eir_dim> dims;
+  for (int i = 0; i < desc->num_dims; ++i) {
+    if (i == cpx) continue;
+    eir_dim y = desc->dims[i];
+    y.stride_right = packed[i];
+    dims.push_back(y);
+  }
+  eir_dim ci{}, co{};
+  ci.type = EIR_DIM_K;
+  ci.size = 2;
+  ci.stride_left = x.stride_left;
+  ci.stride_right = 2 * nb;
+  co.type = EIR_DIM_N;
+  co.size = 2;
+  co.stride_right = nb;
+  co.stride_out = x.stride_out;
+  dims.push_back(ci);
+  dims.push_back(co);
+  eir_contract_desc rd = *desc;
+  rd.num_dims = (int32_t)dims.size();
+  rd.dims = dims.data();
+  rd.ktype_first_touch = desc->ktype_first_touch == EIR_KTYPE_CPX_ZERO ? EIR_KTYPE_ZERO : EIR_KTYPE_UNDEFINED;
+  rd.ktype_main = EIR_KTYPE_MADD;
+  eir_plan *inner = nullptr;
+  int rc = eir_contract_plan_create(&rd, &inner);
+  if (rc != EIR_SUCCESS) return rc;
+
+  eir_plan *p = new eir_plan();
+  p->what = 1;
+  p->dt_l = p->dt_r = p->dt_o = dt;
+  p->comp = desc->dtype_comp;
+  p->first = desc->ktype_first_touch;
+  p->last = desc->ktype_last_touch;
+  p->desc_flags = desc->flags;
+  p->family = inner->family;
+  p->num_ops = inner->num_ops;  // 8|C||M||N||K| - 2|C||M||N| with ZERO: the reference's count
+  p->empty = inner->empty;
+  p->cpx_inner = inner;
+  p->esize = dt == EIR_FP64 ? 8 : 4;
+  p->cpx_stride_right = x.stride_right;
+  eir::PermuteParams &e = p->cpx_expand;
+  e = eir::PermuteParams();
+  e.nd = (int32_t)bdims.size();
+  for (int j = 0; j < e.nd; ++j) {
+    e.size[j] = desc->dims[bdims[j]].size;
+    e.sin[j] = desc->dims[bdims[j]].stride_right;
+    e.sout[j] = packed[bdims[j]];
+  }
+  e.total = nb;
+  p->ws_bytes = 4 * nb * p->esize;
+  p->text = "complex: right operand expanded to [[Br, Bi], [-Bi, Br]] (" + std::to_string(nb) +
+            " x 4 elements) + " + inner->text;
+  *plan_out = p;
+  return EIR_SUCCESS;
+}
+
 int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out) {
   if (desc == nullptr || plan_out == nullptr)
     return set_error(EIR_INVALID_ARGUMENT, "null descriptor or plan pointer");
   *plan_out = nullptr;
   if (desc->num_dims < 0 || (desc->num_dims > 0 && desc->dims == nullptr))
     return set_error(EIR_INVALID_ARGUMENT, "bad dims");
+  for (int i = 0; i < desc->num_dims; ++i)
+    if (desc->dims[i].type == EIR_DIM_CPX) return create_complex_plan(desc, plan_out);
   const int dl = desc->dtype_left, dr = desc->dtype_right, dout = desc->dtype_out;
   bool dt_ok = (dout == EIR_FP64 && dl == EIR_FP64 && dr == EIR_FP64) ||
                (dout == EIR_FP32 && (dl == EIR_FP32 || dl == EIR_BF16) &&
@@ -797,6 +895,28 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   bool uses_aux = p->first == EIR_KTYPE_COPY || p->first == EIR_KTYPE_ADD || p->last == EIR_KTYPE_ADD;
   if (uses_aux && aux == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (p->cpx_inner != nullptr) {
+    // complex: expand the right operand into the workspace, then the real plan
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (p->ws == nullptr || p->ws_device != dev) {
+      if (p->ws != nullptr) cudaFree(p->ws);
+      cudaError_t e = cudaMalloc(&p->ws, (size_t)std::max<int64_t>(p->ws_bytes, 16));
+      if (e != cudaSuccess) {
+        p->ws = nullptr;
+        return cuda_fail(e, "cudaMalloc(workspace)");
+      }
+      p->ws_device = dev;
+    }
+    DeviceState *ds = nullptr;
+    int rc = device_state(&ds);
+    if (rc != EIR_SUCCESS) return rc;
+    cudaError_t e = eir::launch_cpx_expand(p->esize, p->cpx_expand, p->cpx_stride_right, r, p->ws,
+                                           ds->num_sms, st);
+    if (e != cudaSuccess) return cuda_fail(e, "complex expansion launch");
+    g_launches.fetch_add(1, std::memory_order_relaxed);
+    return eir_contract(p->cpx_inner, l, p->ws, aux, out, stream);
+  }
   if (p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA) return run_simt(p, l, r, aux, out, st);
 
   DeviceState *ds = nullptr;
@@ -928,6 +1048,7 @@ int eir_plan_destroy(eir_plan *p) {
     cudaEventDestroy(ev.second);
   }
   if (p->pre) eir_plan_destroy(p->pre);
+  if (p->cpx_inner) eir_plan_destroy(p->cpx_inner);
   if (p->ws) {
     int cur = 0;
     cudaGetDevice(&cur);

@@ -13,6 +13,11 @@ cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const 
 cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,
                            int num_sms, cudaStream_t st);
 
+// right operand of a complex contraction expanded into the real blocks
+// [[Br, Bi], [-Bi, Br]] (esize 4 or 8; p: B's non-complex dims, packed sout)
+cudaError_t launch_cpx_expand(int esize, PermuteParams const &p, int64_t cpx_stride, void const *in,
+                              void *out, int num_sms, cudaStream_t st);
+
 // kind: 0 = BF16 (kind::f16), 1 = TF32, 2 = 3xTF32 (FP32-accurate)
 // ksub: K blocks (128-byte swizzle rows) per ring stage, 1 or 2
 cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,

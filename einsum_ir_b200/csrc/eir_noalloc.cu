@@ -88,6 +88,9 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
     return eir::api_set_error(EIR_NO_DATA_PTR_PROVIDED, "null operand pointer");
   bool uses_aux = p->first == EIR_KTYPE_COPY || p->first == EIR_KTYPE_ADD || p->last == EIR_KTYPE_ADD;
   if (uses_aux && aux == nullptr) return eir::api_set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
+  if (p->cpx_inner != nullptr)
+    return eir::api_set_error(EIR_INVALID_ARGUMENT,
+                              "eir_contract_no_alloc: complex plans need their expansion workspace");
   if (p->prepack >= 0 && (size_t)p->ws_bytes > kStaticOperandBytes) {
     char buf[192];
     std::snprintf(buf, sizeof(buf),

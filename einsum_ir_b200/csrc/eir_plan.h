@@ -63,6 +63,11 @@ struct eir_plan {
   std::vector<eir::LDim> dims;   // after size-1 removal and fusion
   eir::SimtParams simt;
   bool tc = false;
+  // complex contraction: the right operand is expanded into real blocks
+  // (cpx_expand, into the workspace) and `cpx_inner` contracts the real problem
+  eir_plan *cpx_inner = nullptr;
+  eir::PermuteParams cpx_expand;
+  int64_t cpx_stride_right = 0;
   int tc_kind = 0, tc_bn = 128, tc_ksub = 1;
   bool tc_pair = false;  // CTA-pair (cta_group::2) kernel, 256-row tiles
   bool a_mn = false, b_mn = false;

@@ -297,6 +297,50 @@ static bool offsets_fit_int32(PermuteParams const &p) {
          p.total < (int64_t(1) << 31);
 }
 
+// complex contraction operand: B' = [[Br, Bi], [-Bi, Br]] as four packed real
+// blocks (block ci * 2 + co at offset (ci * 2 + co) * nb); p describes B's
+// non-complex dims (sizes, source strides, packed destination strides)
+template <typename T>
+__global__ void __launch_bounds__(256)
+    cpx_expand_kernel(const PermuteParams p, int64_t cpx_stride, const T *__restrict__ in,
+                      T *__restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t nb = p.total;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < nb;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    int64_t r = e, oi = 0, oo = 0;
+#pragma unroll
+    for (int d = 0; d < kMaxPermDims; ++d) {
+      if (d < p.nd) {
+        const int64_t i = r % p.size[d];
+        r /= p.size[d];
+        oi += i * p.sin[d];
+        oo += i * p.sout[d];
+      }
+    }
+    const T re = in[oi], im = in[oi + cpx_stride];
+    out[oo] = re;
+    out[nb + oo] = im;
+    out[2 * nb + oo] = -im;
+    out[3 * nb + oo] = re;
+  }
+}
+
+cudaError_t launch_cpx_expand(int esize, PermuteParams const &p, int64_t cpx_stride, void const *in,
+                              void *out, int num_sms, cudaStream_t st) {
+  if (p.total == 0) return cudaSuccess;
+  int64_t blocks = (p.total + 255) / 256;
+  if (blocks > (int64_t)num_sms * 16) blocks = (int64_t)num_sms * 16;
+  if (esize == 4)
+    return launch_kernel(cpx_expand_kernel<float>, dim3((unsigned)blocks), dim3(256), 0, st, p,
+                         cpx_stride, static_cast<float const *>(in), static_cast<float *>(out));
+  if (esize == 8)
+    return launch_kernel(cpx_expand_kernel<double>, dim3((unsigned)blocks), dim3(256), 0, st, p,
+                         cpx_stride, static_cast<double const *>(in), static_cast<double *>(out));
+  return cudaErrorInvalidValue;
+}
+
 template <typename T>
 static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void *out, int num_sms,
                                     cudaStream_t st) {

@@ -50,8 +50,11 @@ enum {
   EIR_UNDEFINED_ERROR           = 99
 };
 
-/* dimension types: identical values to einsum_ir::dim_t (C, M, N, K) */
-enum { EIR_DIM_C = 0, EIR_DIM_M = 1, EIR_DIM_N = 2, EIR_DIM_K = 3 };
+/* dimension types: identical values to einsum_ir::dim_t (C, M, N, K, CPX).
+ * EIR_DIM_CPX: the complex dimension (size 2: real, imaginary part) of a
+ * complex contraction, present in left, right and out (dim_t::CPX,
+ * src/constants.h:13); it needs ktype_main EIR_KTYPE_CPX_MADD. */
+enum { EIR_DIM_C = 0, EIR_DIM_M = 1, EIR_DIM_N = 2, EIR_DIM_K = 3, EIR_DIM_CPX = 4 };
 
 /* data types: FP32/FP64 keep einsum_ir::data_t values; BF16 is an extension */
 enum { EIR_FP32 = 0, EIR_FP64 = 1, EIR_BF16 = 2, EIR_UNDEFINED_DTYPE = 99 };
@@ -65,10 +68,11 @@ enum {
   EIR_COMPUTE_BF16    = 4  /* BF16 multiplicands, FP32 accumulate */
 };
 
-/* kernel types: identical values to einsum_ir::kernel_t (real subset) */
+/* kernel types: identical values to einsum_ir::kernel_t (the real kernels and
+ * the complex zero / multiply-add pair, src/constants.h:60-76) */
 enum {
   EIR_KTYPE_ZERO = 0, EIR_KTYPE_RELU = 1, EIR_KTYPE_ADD = 2, EIR_KTYPE_COPY = 3,
-  EIR_KTYPE_MADD = 4, EIR_KTYPE_UNDEFINED = 99
+  EIR_KTYPE_MADD = 4, EIR_KTYPE_CPX_ZERO = 6, EIR_KTYPE_CPX_MADD = 8, EIR_KTYPE_UNDEFINED = 99
 };
 
 /* kernel family chosen by the planner (eir_plan_kernel_family) */
