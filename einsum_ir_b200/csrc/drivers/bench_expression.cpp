@@ -6,7 +6,9 @@
 // Command line as the reference driver (src/bench_expression.cpp:8-31):
 //   bench_expression einsum_string dimension_sizes contraction_path [dtype [store_lock [print_tree]]]
 // dtype: FP32 (default), FP64, BF16 (BF16 inputs, FP32 accumulation and
-// output) or TF32 (FP32 data, single-pass TF32 tensor-core compute).
+// output), TF32 (FP32 data, single-pass TF32 tensor-core compute), CPX_FP32 or
+// CPX_FP64 (complex, interleaved: a size-2 dim appended to every tensor as in
+// src/bench_expression.cpp:110-247).
 // Differences: data are seeded uniform [-1, 1) values (the reference draws
 // at::randn); the eval time is the mean over a CUDA-event-timed loop (the
 // reference times one eval with a host clock); the check solution is the
@@ -38,7 +40,7 @@ void usage() {
                "  * einsum_string:    Einsum expression string. Either in single-character or standard format.\n"
                "  * dimension_sizes:  Dimension sizes have to be in ascending order of the dimension names.\n"
                "  * contraction_path: Contraction path.\n"
-               "  * dtype:            FP32, FP64, BF16 or TF32, default: FP32.\n"
+               "  * dtype:            FP32, FP64, BF16, TF32, CPX_FP32 or CPX_FP64, default: FP32.\n"
                "  * store_lock:       If 1 all input tensors are stored and locked before evaluation, default: 0.\n"
                "  * print_tree:       If not 0 the contraction tree is printed (1: dimension ids, 2: names), default: 0.\n\n"
                "Example:\n"
@@ -120,11 +122,21 @@ int main(int argc, char *argv[]) {
   std::printf("\n");
 
   std::string dtype = argc > 4 ? std::string(argv[4]) : std::string("FP32");
-  if (dtype != "FP32" && dtype != "FP64" && dtype != "BF16" && dtype != "TF32") {
+  einsum_ir::complex_t ctype = einsum_ir::UNDEFINED_CTYPE;
+  EinsumExpressionAscii::parse_ctype(dtype, ctype);
+  if (ctype == einsum_ir::UNDEFINED_CTYPE && dtype != "TF32") {
     std::fprintf(stderr, "failed to determine dtype\n");
     return EXIT_FAILURE;
   }
+  const bool cpx = ctype == einsum_ir::BATCH_INNER;
   std::printf("dtype: %s\n", dtype.c_str());
+  std::printf("ctype: %s\n", cpx ? "BATCH_INNER" : "REAL_ONLY");
+  // complex: one more dim (size 2, the largest id) innermost in every tensor
+  const int64_t cpx_id = (int64_t)name_to_id.size();
+  if (cpx) {
+    tr.dim_sizes.push_back(2);
+    id_to_name[cpx_id] = "(cpx)";
+  }
   const bool store_lock = argc > 5 && std::stoi(argv[5]) == 1;
   std::printf("store_lock: %d\n", store_lock ? 1 : 0);
   const int print_tree = argc > 6 ? std::stoi(argv[6]) : 0;
@@ -147,14 +159,19 @@ int main(int argc, char *argv[]) {
       tr.string_dim_ids.push_back(name_to_id[n]);
       shape.push_back(tr.dim_sizes[name_to_id[n]]);
     }
-    tr.string_num_dims.push_back((int64_t)names.size());
+    if (cpx) {
+      tr.string_dim_ids.push_back(cpx_id);
+      shape.push_back(2);
+    }
+    tr.string_num_dims.push_back((int64_t)names.size() + (cpx ? 1 : 0));
     tr.shapes.push_back(shape);
   }
 
   // ---- data: seeded uniform inputs, stored in the run's input type
-  const int in_esize = dtype == "FP64" ? 8 : (dtype == "BF16" ? 2 : 4);
-  const int out_esize = dtype == "FP64" ? 8 : 4;
-  const einsum_ir::data_t dt = dtype == "FP64" ? einsum_ir::FP64 : einsum_ir::FP32;
+  const bool fp64 = dtype == "FP64" || dtype == "CPX_FP64";
+  const int in_esize = fp64 ? 8 : (dtype == "BF16" ? 2 : 4);
+  const int out_esize = fp64 ? 8 : 4;
+  const einsum_ir::data_t dt = fp64 ? einsum_ir::FP64 : einsum_ir::FP32;
   std::vector<DeviceTensor> dev(tr.num_tensors);
   std::vector<std::vector<double>> held(tr.num_tensors);
   std::vector<void *> ptrs(tr.num_tensors);
@@ -175,7 +192,8 @@ int main(int argc, char *argv[]) {
   if (dtype == "BF16") exp.set_input_dtype(einsum_ir::BF16);
   if (dtype == "TF32") exp.set_compute_type(EIR_COMPUTE_TF32);
   exp.init((int64_t)tr.dim_sizes.size(), tr.dim_sizes.data(), tr.num_tensors - 2,
-           tr.string_num_dims.data(), tr.string_dim_ids.data(), tr.path.data(), dt, ptrs.data());
+           tr.string_num_dims.data(), tr.string_dim_ids.data(), tr.path.data(),
+           cpx ? einsum_ir::BATCH_INNER : einsum_ir::REAL_ONLY, dt, ptrs.data());
   exp.set_stream(st);
   auto tp0 = std::chrono::steady_clock::now();
   einsum_ir::err_t err = exp.compile();
@@ -241,8 +259,8 @@ int main(int argc, char *argv[]) {
     CudaCoreOnly guard;
     EinsumExpression ref_exp;
     ref_exp.init((int64_t)tr.dim_sizes.size(), tr.dim_sizes.data(), tr.num_tensors - 2,
-                 tr.string_num_dims.data(), tr.string_dim_ids.data(), tr.path.data(), einsum_ir::FP64,
-                 ref_ptrs.data());
+                 tr.string_num_dims.data(), tr.string_dim_ids.data(), tr.path.data(),
+                 cpx ? einsum_ir::BATCH_INNER : einsum_ir::REAL_ONLY, einsum_ir::FP64, ref_ptrs.data());
     ref_exp.set_stream(st);
     if (ref_exp.compile() != einsum_ir::SUCCESS || ref_exp.eval() != EIR_SUCCESS) {
       std::fprintf(stderr, "error: FP64 check solution failed: %s\n", eir_last_error_string());
@@ -254,7 +272,7 @@ int main(int argc, char *argv[]) {
   std::printf("\n*** comparing solution ***:\n");
   ErrorReport r = compare(ref, got);
   print_report(r, "FP64 CUDA-core solution");
-  const double tol = dtype == "FP64" ? 1e-12 : (dtype == "TF32" ? 1e-2 : 1e-5);
+  const double tol = fp64 ? 1e-12 : (dtype == "TF32" ? 1e-2 : 1e-5);
   cudaStreamDestroy(st);
   if (r.rel > tol) {
     std::fprintf(stderr, "warning: relative error is large!\n");

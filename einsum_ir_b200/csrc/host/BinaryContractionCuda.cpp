@@ -13,8 +13,20 @@ err_t BinaryContractionCuda::compile() {
   err_t err = compile_base();
   if (err != SUCCESS) return err;
   if (m_num_dims_i > 0 || m_num_dims_j > 0) return COMPILATION_FAILED;  // no one-sided sums
-  if (ce_cpx_op(m_ktype_first_touch) || ce_cpx_op(m_ktype_main) || ce_cpx_op(m_ktype_last_touch))
+  // complex contractions: CPX_ZERO (or accumulate) + CPX_MADD, no last touch.
+  // The complex dim is the size-2 C dim with the largest id (the frontends add
+  // it after the real dims, src/bench_expression.cpp:110).
+  const bool cpx = m_ktype_main == CPX_MADD;
+  if (cpx ? ((m_ktype_first_touch != CPX_ZERO && m_ktype_first_touch != UNDEFINED_KTYPE) ||
+             m_ktype_last_touch != UNDEFINED_KTYPE)
+          : (ce_cpx_op(m_ktype_first_touch) || ce_cpx_op(m_ktype_main) || ce_cpx_op(m_ktype_last_touch)))
     return INVALID_KTYPE;
+  int64_t cpx_id = -1;
+  if (cpx) {
+    for (size_t d = 0; d < m_dim_ids_c.size(); ++d)
+      if (m_sizes_c[d] == 2 && m_dim_ids_c[d] > cpx_id) cpx_id = m_dim_ids_c[d];
+    if (cpx_id < 0) return INVALID_CPX_DIM;
+  }
 
   // strides as in the reference backends (BinaryContractionTpp.cpp:12-42): row-major
   // from the outer sizes; the aux tensor uses its own outer sizes, or the output's
@@ -36,7 +48,7 @@ err_t BinaryContractionCuda::compile() {
   auto add = [&](std::vector<int64_t> const &ids, std::vector<int64_t> const &sizes, int32_t type) {
     for (size_t d = 0; d < ids.size(); ++d) {
       eir_dim x{};
-      x.type = type;
+      x.type = ids[d] == cpx_id ? EIR_DIM_CPX : type;
       x.size = sizes[d];
       x.stride_left = get(sl, ids[d]);
       x.stride_right = get(sr, ids[d]);
@@ -68,6 +80,7 @@ err_t BinaryContractionCuda::compile() {
   int rc = eir_contract_plan_create(&desc, &m_plan);
   if (rc != EIR_SUCCESS) return rc == EIR_INVALID_DTYPE ? INVALID_DTYPE
                                 : rc == EIR_INVALID_KTYPE ? INVALID_KTYPE
+                                : rc == EIR_INVALID_CPX_DIM ? INVALID_CPX_DIM
                                                           : COMPILATION_FAILED;
   m_compiled = true;
   return SUCCESS;

