@@ -3,18 +3,20 @@
 //
 // Same lowering as the tcgen05 kernel (TcParams, 5-D TMA tensor maps over the
 // operands' native strides, tile loops and outer K loops, fused first/last
-// touch), but tcgen05 has no FP64 kind, so the math runs on warp-level DMMA:
-// warp 0 streams 128-row operand tiles with TMA (128B swizzle, K blocks of 16
-// doubles) into a 4-stage ring; warps 1..8 each own a 64 x 32 slice of the
-// 128 x 128 output tile, read A/B fragments from the swizzled stages
-// (K-major or MN-major, by address arithmetic) and keep the accumulator in
-// registers. Semantics: reference loop engine (ContractionBackend.cpp:296-348,
-// 495-515; ContractionBackendTpp.cpp:80-163).
+// touch), but tcgen05 has no FP64 kind, so the math runs on warp-level DMMA.
+// Warp-specialised: warpgroup 0 gives its registers away (setmaxnreg) and one
+// of its threads streams 128-row operand tiles with TMA (128B swizzle, K
+// blocks of 16 doubles) into a 4-stage ring; warpgroups 1 and 2 (8 warps)
+// each own a 32 x 64 slice of the 128 x 128 output tile, read A/B fragments
+// from the swizzled stages (K-major or MN-major, by address arithmetic) and
+// keep the accumulator in registers. Semantics: reference loop engine
+// (ContractionBackend.cpp:296-348, 495-515; ContractionBackendTpp.cpp:80-163).
 #include <cuda.h>
 #include "eir_common.cuh"
 #include "eir_params.h"
 #include "eir_kernels.h"
 #include "eir_launch.h"
+#include "tc_tile.cuh"
 
 namespace eir {
 
@@ -23,69 +25,69 @@ namespace {
 constexpr int kDmmaBM = 128, kDmmaBN = 128, kDmmaBK = 16;  // 16 doubles = one 128-byte row
 constexpr int kDmmaStages = 4;
 constexpr int kDmmaTileBytes = 128 * 128;                   // one operand tile per stage
-constexpr int kDmmaMathWarps = 16;  // 4 (M) x 4 (N) warps, 32 x 32 outputs each
-constexpr int kDmmaThreads = 32 * (1 + kDmmaMathWarps);
+// 4 (M) x 2 (N) math warps, 32 x 64 outputs each (64 doubles of accumulator
+// per thread). The register file is split over the 4 SM sub-partitions, so a
+// launch's per-thread registers follow from its warps per sub-partition: 12
+// warps (3 warpgroups) launch with 168; the producer warpgroup drops to 56 and
+// the two math warpgroups rise to 224, which adds up to the launch's total
+// (128 x 56 + 256 x 224 = 384 x 168). A 9-warp launch would cap the math at
+// 168 registers and a 17-warp one at 96, both of which spill.
+constexpr int kDmmaWarpsM = 4, kDmmaWarpsN = 2;
+constexpr int kDmmaMathWarps = kDmmaWarpsM * kDmmaWarpsN;
+constexpr int kDmmaThreads = 128 + 32 * kDmmaMathWarps;
+constexpr int kDmmaLaunchRegs = 168, kDmmaProducerRegs = 56, kDmmaMathRegs = 224;
+static_assert(kDmmaThreads == 384 && 65536 / kDmmaThreads / 8 * 8 == kDmmaLaunchRegs, "launch registers");
+static_assert(128 * kDmmaProducerRegs + 32 * kDmmaMathWarps * kDmmaMathRegs <= kDmmaThreads * kDmmaLaunchRegs,
+              "register split exceeds the launch's registers");
+constexpr int kDmmaWI = kDmmaBM / kDmmaWarpsM / 8, kDmmaWJ = kDmmaBN / kDmmaWarpsN / 8;
 constexpr int kDmmaSmem = 1024 + kDmmaStages * 2 * kDmmaTileBytes + 256;
 
-// byte offset of element (row r, k) of a K-major 128B-swizzled tile [128 rows][16 doubles]
-__device__ __forceinline__ uint32_t kmajor_off(int r, int k) {
-  return (uint32_t)(r * 128 + ((((k >> 1) ^ (r & 7)) << 4) | ((k & 1) << 3)));
-}
-// byte offset of element (row r, k) of an MN-major tile: 8 boxes [16 k][16 rows]
-__device__ __forceinline__ uint32_t mnmajor_off(int r, int k) {
-  int b = r >> 4, rr = r & 15;
-  return (uint32_t)(b * 2048 + k * 128 + ((((rr >> 1) ^ (k & 7)) << 4) | ((rr & 1) << 3)));
-}
-
 __device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b) {
-  asm volatile("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
+  asm("mma.sync.aligned.m8n8k4.row.col.f64.f64.f64.f64 {%0, %1}, {%2}, {%3}, {%0, %1};"
                : "+d"(c0), "+d"(c1)
                : "d"(a), "d"(b));
 }
 
-struct DTile {
-  int64_t mt, nt;
-  int64_t l[kMaxTileLoops];
-};
-
-__device__ __forceinline__ DTile decode_dtile(TcParams const &p, int64_t t) {
-  DTile c;
-  const int64_t mn = (int64_t)p.m_tiles * p.n_tiles;
-  int64_t u = t % mn;
-  t /= mn;
-  const int64_t gfull = (int64_t)p.group_m * p.n_tiles;
-  const int64_t g = u / gfull;
-  const int64_t first_m = g * p.group_m;
-  const int64_t rem = p.m_tiles - first_m;
-  const int64_t gm = rem < p.group_m ? rem : p.group_m;
-  const int64_t r = u - g * gfull;
-  c.mt = first_m + r % gm;
-  c.nt = r / gm;
-#pragma unroll
-  for (int i = 0; i < kMaxTileLoops; ++i) {
-    if (i < p.n_loops) {
-      c.l[i] = t % p.loop_size[i];
-      t /= p.loop_size[i];
-    } else {
-      c.l[i] = 0;
-    }
-  }
-  return c;
-}
-
-__device__ __forceinline__ int dsrc(int8_t src, int64_t ko0, int64_t ko1, DTile const &c) {
-  switch (src) {
-    case kSrcKo0: return (int)ko0;
-    case kSrcKo1: return (int)ko1;
-    case kSrcLoop0: return (int)c.l[0];
-    case kSrcLoop0 + 1: return (int)c.l[1];
-    case kSrcLoop0 + 2: return (int)c.l[2];
-    case kSrcLoop0 + 3: return (int)c.l[3];
-    default: return 0;
-  }
-}
-
 }  // namespace
+
+// Per-thread byte offsets of the DMMA fragments in one stage. A thread reads
+// rows w + x * 8 + g (x = fragment index, g = lane / 4) at k = 4 tq + 2 h + q
+// (tq = lane % 4, h = K half, q = 0, 1); in the 128B swizzle these offsets are a
+// thread constant plus an immediate per x:
+//  K-major  [rows][16 doubles]: rows are 128 B and the 16-byte chunk index
+//           (k / 2) ^ (row % 8) = (2 tq + h) ^ g does not depend on x, so
+//           off = base[h] + x * 1024 and one 128-bit load fetches q = 0, 1;
+//  MN-major 8 boxes [16 k][16 rows]: off = box * 2048 + k * 128 + chunk * 16
+//           + (row % 2) * 8 with chunk = ((row % 16) / 2) ^ (k % 8); x moves
+//           the box by x / 2 and flips chunk bit 2 (byte bit 6) by x % 2.
+template <bool MN>
+struct FragOffsets {
+  uint32_t base[2][2];  // [h][q]; K-major uses base[h][0] only
+  __device__ __forceinline__ FragOffsets(int w, int g, int tq) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h)
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        const int k = 4 * tq + 2 * h + q;
+        if (MN)
+          base[h][q] = (uint32_t)((w >> 4) * 2048 + k * 128 + ((((g >> 1) ^ (k & 7))) << 4) + ((g & 1) << 3));
+        else
+          base[h][q] = (uint32_t)((w + g) * 128 + (((2 * tq + h) ^ g) << 4));
+      }
+  }
+  // the pair (k, k + 1) of fragment x in K half h
+  __device__ __forceinline__ double2 load(uint8_t const *tile, int h, int x) const {
+    double2 v;
+    if (MN) {
+      const uint32_t flip = (uint32_t)(x & 1) << 6, box = (uint32_t)(x >> 1) * 2048;
+      v.x = *reinterpret_cast<const double *>(tile + ((base[h][0] ^ flip) + box));
+      v.y = *reinterpret_cast<const double *>(tile + ((base[h][1] ^ flip) + box));
+    } else {
+      v = *reinterpret_cast<const double2 *>(tile + base[h][0] + x * 1024);
+    }
+    return v;
+  }
+};
 
 template <bool A_MN, bool B_MN>
 __global__ void __launch_bounds__(kDmmaThreads, 1)
@@ -93,13 +95,14 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
                          const __grid_constant__ CUtensorMap map_b, const TcParams p,
                          const double *__restrict__ aux, double *__restrict__ out) {
   extern __shared__ uint8_t smem_raw[];
-  uint8_t *smem = reinterpret_cast<uint8_t *>(
-      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // 1024-byte alignment by offsetting the shared array itself, so that the
+  // compiler still knows the fragment loads are shared-memory loads
+  uint8_t *smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
   uint8_t *sA = smem;
   uint8_t *sB = smem + kDmmaStages * kDmmaTileBytes;
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + 2 * kDmmaStages * kDmmaTileBytes);
   uint64_t *full = bars;                 // kDmmaStages
-  uint64_t *empty = bars + kDmmaStages;  // kDmmaStages (8 MMA warps arrive)
+  uint64_t *empty = bars + kDmmaStages;  // kDmmaStages (the math warps arrive)
   volatile int *abort_flag = reinterpret_cast<volatile int *>(bars + 2 * kDmmaStages);
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -116,45 +119,45 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
   pdl_wait();  // operands / output may come from the previous kernel of the stream
   const int k_steps = p.k_steps;
 
-  if (warp == 0) {
-    if (lane == 0) {
+  if (warp < 4) {
+    // ---- producer warpgroup: one thread issues every TMA load ----
+    setmaxnreg_dec<kDmmaProducerRegs>();
+    if (warp == 0 && lane == 0) {
       tma_prefetch_map(&map_a);
       tma_prefetch_map(&map_b);
       int stage = 0;
       uint32_t phase = 0;
       for (int64_t t = blockIdx.x; t < p.total_tiles && !*abort_flag; t += gridDim.x) {
-        DTile c = decode_dtile(p, t);
-        const int mrow = (int)(c.mt * kDmmaBM), nrow = (int)(c.nt * kDmmaBN);
-        for (int ks = 0; ks < k_steps; ++ks) {
+        // rotated, division-free K walk (the sum over K is order free)
+        ProducerTile pt = producer_tile<1>(p, t, k_steps, kDmmaBM, 0, kDmmaBN, 0);
+        for (int js = 0; js < k_steps; ++js) {
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
             if (!*abort_flag) record_error(p.err, kErrTimeoutProducer);
             *abort_flag = 1;
             break;
           }
-          const int kp = ks % p.kp_blocks;
-          const int64_t r = ks / p.kp_blocks;
-          const int64_t ko0 = r % p.ko_size[0], ko1 = r / p.ko_size[0];
           mbar_arrive_expect_tx(&full[stage], 2 * kDmmaTileBytes);
           uint8_t *dA = sA + stage * kDmmaTileBytes, *dB = sB + stage * kDmmaTileBytes;
-          const int kcol = kp * kDmmaBK;
-          const int a2 = dsrc(p.a_src[2], ko0, ko1, c), a3 = dsrc(p.a_src[3], ko0, ko1, c),
-                    a4 = dsrc(p.a_src[4], ko0, ko1, c);
-          const int b2 = dsrc(p.b_src[2], ko0, ko1, c), b3 = dsrc(p.b_src[3], ko0, ko1, c),
-                    b4 = dsrc(p.b_src[4], ko0, ko1, c);
+          const int kcol = pt.kw.kp * kDmmaBK, ko0 = pt.kw.ko0, ko1 = pt.kw.ko1;
+          const int a2 = slot_at(pt.sa, 0, ko0, ko1), a3 = slot_at(pt.sa, 1, ko0, ko1),
+                    a4 = slot_at(pt.sa, 2, ko0, ko1);
+          const int b2 = slot_at(pt.sb, 0, ko0, ko1), b3 = slot_at(pt.sb, 1, ko0, ko1),
+                    b4 = slot_at(pt.sb, 2, ko0, ko1);
           if (!A_MN) {
-            tma_load_5d(dA, &map_a, &full[stage], kcol, mrow, a2, a3, a4);
+            tma_load_5d(dA, &map_a, &full[stage], kcol, pt.mrow, a2, a3, a4);
           } else {
 #pragma unroll
             for (int j = 0; j < kDmmaBM / 16; ++j)
-              tma_load_5d(dA + j * 2048, &map_a, &full[stage], mrow + j * 16, kcol, a2, a3, a4);
+              tma_load_5d(dA + j * 2048, &map_a, &full[stage], pt.mrow + j * 16, kcol, a2, a3, a4);
           }
           if (!B_MN) {
-            tma_load_5d(dB, &map_b, &full[stage], kcol, nrow, b2, b3, b4);
+            tma_load_5d(dB, &map_b, &full[stage], kcol, pt.nrow, b2, b3, b4);
           } else {
 #pragma unroll
             for (int j = 0; j < kDmmaBN / 16; ++j)
-              tma_load_5d(dB + j * 2048, &map_b, &full[stage], nrow + j * 16, kcol, b2, b3, b4);
+              tma_load_5d(dB + j * 2048, &map_b, &full[stage], pt.nrow + j * 16, kcol, b2, b3, b4);
           }
+          pt.kw.next(p);
           if (++stage == kDmmaStages) {
             stage = 0;
             phase ^= 1u;
@@ -163,16 +166,19 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
       }
     }
   } else {
-    // 16 math warps: 4 (M) x 4 (N), warp tile 32 x 32 = 4 x 4 DMMA tiles of 8 x 8
-    constexpr int WI = 4, WJ = 4;
-    const int mw = warp - 1;
-    const int wm = (mw & 3) * 32, wn = (mw >> 2) * 32;
+    // ---- math warpgroups ----
+    setmaxnreg_inc<kDmmaMathRegs>();
+    // warp tile (8 WI) x (8 WJ) = WI x WJ DMMA tiles of 8 x 8
+    constexpr int WI = kDmmaWI, WJ = kDmmaWJ;
+    const int mw = warp - 4;
+    const int wm = (mw % kDmmaWarpsM) * (8 * WI), wn = (mw / kDmmaWarpsM) * (8 * WJ);
     const int g = lane >> 2, tq = lane & 3;
+    const FragOffsets<A_MN> fa(wm, g, tq);
+    const FragOffsets<B_MN> fb(wn, g, tq);
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-      DTile c = decode_dtile(p, t);
       double acc[WI][WJ][2];
 #pragma unroll
       for (int i = 0; i < WI; ++i)
@@ -184,23 +190,26 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
           break;
         }
         const uint8_t *tA = sA + stage * kDmmaTileBytes, *tB = sB + stage * kDmmaTileBytes;
+        // The sum over the block's 16 k is order free: MMA k-slot tq takes the
+        // physical k = 4 tq + 2 h + q over the four MMAs (h, q), so a thread's
+        // values for q = 0, 1 share one 16-byte chunk of a K-major tile.
 #pragma unroll
-        for (int kk = 0; kk < kDmmaBK; kk += 4) {
-          double a[WI], b[WJ];
+        for (int h = 0; h < 2; ++h) {
+          double2 a[WI], b[WJ];
 #pragma unroll
-          for (int i = 0; i < WI; ++i) {
-            const int r = wm + i * 8 + g, k = kk + tq;
-            a[i] = *reinterpret_cast<const double *>(tA + (A_MN ? mnmajor_off(r, k) : kmajor_off(r, k)));
-          }
+          for (int i = 0; i < WI; ++i) a[i] = fa.load(tA, h, i);
 #pragma unroll
-          for (int j = 0; j < WJ; ++j) {
-            const int r = wn + j * 8 + g, k = kk + tq;
-            b[j] = *reinterpret_cast<const double *>(tB + (B_MN ? mnmajor_off(r, k) : kmajor_off(r, k)));
-          }
+          for (int j = 0; j < WJ; ++j) b[j] = fb.load(tB, h, j);
+          // two passes of WI * WJ independent DMMAs: an accumulator is revisited
+          // only after all the others, which hides the DMMA latency
 #pragma unroll
           for (int i = 0; i < WI; ++i)
 #pragma unroll
-            for (int j = 0; j < WJ; ++j) dmma(acc[i][j][0], acc[i][j][1], a[i], b[j]);
+            for (int j = 0; j < WJ; ++j) dmma(acc[i][j][0], acc[i][j][1], a[i].x, b[j].x);
+#pragma unroll
+          for (int i = 0; i < WI; ++i)
+#pragma unroll
+            for (int j = 0; j < WJ; ++j) dmma(acc[i][j][0], acc[i][j][1], a[i].y, b[j].y);
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(&empty[stage]);
@@ -211,21 +220,22 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
       }
       if (!ok) break;
       // epilogue: fragment element (row g, cols 2tq, 2tq+1) of each 8 x 8 tile
+      const TileCoord c = decode_tile(p, t);
       int64_t lo = 0, la = 0;
 #pragma unroll
       for (int i = 0; i < kMaxTileLoops; ++i) {
-        lo += c.l[i] * p.loop_so[i];
-        la += c.l[i] * p.loop_sa[i];
+        lo += (int64_t)c.l[i] * p.loop_so[i];
+        la += (int64_t)c.l[i] * p.loop_sa[i];
       }
 #pragma unroll
       for (int i = 0; i < WI; ++i) {
-        const int64_t m = c.mt * kDmmaBM + wm + i * 8 + g;
+        const int64_t m = (int64_t)c.mt * kDmmaBM + wm + i * 8 + g;
         const bool mok = m < p.m_size;
 #pragma unroll
         for (int j = 0; j < WJ; ++j) {
 #pragma unroll
           for (int h = 0; h < 2; ++h) {
-            const int64_t n = c.nt * kDmmaBN + wn + j * 8 + 2 * tq + h;
+            const int64_t n = (int64_t)c.nt * kDmmaBN + wn + j * 8 + 2 * tq + h;
             if (mok && n < p.n_size) {
               const int64_t o = lo + m * p.so_m + n * p.so_n;
               const int64_t a = la + m * p.sa_m + n * p.sa_n;
@@ -257,7 +267,14 @@ static cudaError_t launch_dmma_t(CUtensorMap const &ma, CUtensorMap const &mb, T
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev >= 32 || !(attr_set_mask & (1u << dev))) {
-    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDmmaSmem);
+    // the kernel's register split (setmaxnreg) is only sound for the launch
+    // register count it was written for: with fewer, the math warpgroups'
+    // increase could never be granted, so refuse to launch
+    cudaFuncAttributes fa;
+    cudaError_t e = cudaFuncGetAttributes(&fa, kern);
+    if (e != cudaSuccess) return e;
+    if (fa.numRegs != kDmmaLaunchRegs) return cudaErrorInvalidConfiguration;
+    e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, kDmmaSmem);
     if (e != cudaSuccess) return e;
     if (dev < 32) attr_set_mask |= (1u << dev);
   }
