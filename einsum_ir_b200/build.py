@@ -42,7 +42,7 @@ def _sources():
 def _compile(src: Path, verbose: bool) -> Path:
     obj = BUILD / (src.relative_to(CSRC).as_posix().replace("/", "__") + ".o")
     deps = [src] + sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + \
-        sorted((CSRC / "host").glob("*.h")) + [ROOT / "include" / "eir_cuda.h"]
+        sorted((CSRC / "host").glob("*.h")) + sorted((ROOT / "include").glob("*.h"))
     if obj.exists() and all(obj.stat().st_mtime >= d.stat().st_mtime for d in deps if d.exists()):
         return obj
     cmd = [_nvcc(), *ARCH, *COMMON, "-c", str(src), "-o", str(obj)]

@@ -32,7 +32,10 @@ EXPORTS = [
     "eir_expression_eval", "eir_expression_num_ops", "eir_expression_num_tensors",
     "eir_expression_tensor_dims", "eir_expression_destroy", "eir_expression_describe",
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
-    "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc",
+    "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc", "eir_unary_plan_create",
+    # include/eir_tensor_operation.h
+    "eir_top_create", "eir_top_destroy", "eir_top_setup", "eir_top_execute", "eir_top_plan",
+    "eir_top_default_optimization_config", "eir_top_optimize",
 ]
 
 
@@ -74,6 +77,22 @@ def lib() -> ctypes.CDLL:
         L.eir_permute_plan_create.argtypes = [c_int32, POINTER(c_int64), POINTER(c_int64),
                                               POINTER(c_int64), c_int32, POINTER(c_void_p)]
         L.eir_permute.argtypes = [c_void_p] * 4
+        L.eir_unary_plan_create.argtypes = [c_int32, POINTER(c_int64), POINTER(c_int64),
+                                            POINTER(c_int64), c_int32, c_int32, POINTER(c_void_p)]
+        L.eir_top_create.argtypes = [POINTER(c_void_p)]
+        L.eir_top_destroy.argtypes = [c_void_p]
+        L.eir_top_setup.argtypes = [c_void_p, c_int32, c_int32, c_int32, c_int32, c_int32,
+                                    POINTER(c_int32), POINTER(c_int32), POINTER(c_int64), c_int32,
+                                    POINTER(c_int32), POINTER(c_int32), POINTER(c_int64)]
+        L.eir_top_execute.argtypes = [c_void_p] * 5
+        L.eir_top_plan.argtypes = [c_void_p]
+        L.eir_top_plan.restype = c_void_p
+        L.eir_top_default_optimization_config.argtypes = [c_void_p]
+        L.eir_top_optimize.argtypes = [c_int32, c_int32, c_int32, c_int32, c_int32,
+                                       POINTER(c_int32), POINTER(c_int32), POINTER(c_int64), c_int32,
+                                       POINTER(c_int32), POINTER(c_int32), POINTER(c_int64), c_void_p,
+                                       POINTER(c_int32), POINTER(c_int32), POINTER(c_int32),
+                                       POINTER(c_int64), POINTER(c_int32), POINTER(c_int64)]
         L.eir_plan_destroy.argtypes = [c_void_p]
         L.eir_plan_kernel_family.argtypes = [c_void_p]
         L.eir_plan_workspace_bytes.argtypes = [c_void_p]
@@ -124,8 +143,12 @@ def _ptr(x) -> c_void_p:
 
 
 class Plan:
-    def __init__(self, handle: c_void_p):
+    """A plan handle. owned=False: a view of a plan that another object owns
+    (closing the view does not destroy the plan)."""
+
+    def __init__(self, handle: c_void_p, owned: bool = True):
         self._h = handle
+        self._owned = owned
 
     @property
     def handle(self) -> c_void_p:
@@ -153,9 +176,9 @@ class Plan:
         return float(ms.value), int(n.value)
 
     def close(self) -> None:
-        if self._h:
+        if self._h and self._owned:
             lib().eir_plan_destroy(self._h)
-            self._h = None
+        self._h = None
 
     def __del__(self):
         try:

@@ -999,10 +999,25 @@ int eir_permute_plan_create(int32_t nd, int64_t const *sizes, int64_t const *sin
   return EIR_SUCCESS;
 }
 
+int eir_unary_plan_create(int32_t nd, int64_t const *sizes, int64_t const *sin, int64_t const *sout,
+                          int32_t dtype, int32_t ktype, eir_plan **plan_out) {
+  if (ktype == EIR_KTYPE_COPY) return eir_permute_plan_create(nd, sizes, sin, sout, dtype, plan_out);
+  if (plan_out == nullptr) return set_error(EIR_INVALID_ARGUMENT, "null plan pointer");
+  *plan_out = nullptr;
+  if (ktype != EIR_KTYPE_ZERO) return set_error(EIR_INVALID_KTYPE, "unary kernel must be COPY or ZERO");
+  // ZERO: a row plan over the output's strides alone
+  int rc = eir_permute_plan_create(nd, sizes, sout, sout, dtype, plan_out);
+  if (rc != EIR_SUCCESS) return rc;
+  (*plan_out)->unary_zero = true;
+  (*plan_out)->text = "zero: " + (*plan_out)->text;
+  return EIR_SUCCESS;
+}
+
 int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
   if (p == nullptr || p->what != 2) return set_error(EIR_INVALID_ARGUMENT, "not a permute plan");
   if (p->perm.total == 0) return EIR_SUCCESS;
-  if (in == nullptr || out == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null pointer");
+  if ((in == nullptr && !p->unary_zero) || out == nullptr)
+    return set_error(EIR_NO_DATA_PTR_PROVIDED, "null pointer");
   DeviceState *ds = nullptr;
   int rc = device_state(&ds);
   if (rc != EIR_SUCCESS) return rc;
@@ -1012,7 +1027,7 @@ int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
     pp.vec = 1;
   ProfScope prof(p, static_cast<cudaStream_t>(stream));
   cudaError_t e = eir::launch_permute(p->esize, pp, in, out, ds->num_sms,
-                                      static_cast<cudaStream_t>(stream));
+                                      static_cast<cudaStream_t>(stream), p->unary_zero);
   if (e != cudaSuccess) return cuda_fail(e, "permute launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;

@@ -10,8 +10,10 @@ namespace eir {
 cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const &p, void const *l,
                                  void const *r, void const *aux, void *out, cudaStream_t st);
 
+// zero: the unary ZERO primitive (out = 0 over p's output strides, `in` unused;
+// p must be a row-copy plan, which planning with sin = sout gives)
 cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,
-                           int num_sms, cudaStream_t st);
+                           int num_sms, cudaStream_t st, bool zero = false);
 
 // right operand of a complex contraction expanded into the real blocks
 // [[Br, Bi], [-Bi, Br]] (esize 4 or 8; p: B's non-complex dims, packed sout)

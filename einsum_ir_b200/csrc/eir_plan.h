@@ -84,8 +84,9 @@ struct eir_plan {
   int64_t ws_bytes = 0;
   int ws_device = -1;
 
-  // ---- permute
+  // ---- permute (unary COPY) or unary ZERO
   eir::PermuteParams perm;
+  bool unary_zero = false;
   int esize = 4;
 
   // ---- main-kernel timing (eir_plan_profile)

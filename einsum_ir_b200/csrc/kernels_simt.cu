@@ -206,8 +206,9 @@ cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const 
 }
 
 // ------------------------------------------------------------------ permute
-// copy mode: dim 0 is stride-1 in input and output; V elements per access
-template <typename T, int V>
+// copy mode: dim 0 is stride-1 in input and output; V elements per access.
+// ZERO: the unary ZERO primitive (out = 0 over the output's strides; `in` unused)
+template <typename T, int V, bool ZERO>
 __global__ void __launch_bounds__(256)
     permute_copy_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
   struct alignas(sizeof(T) * V) Vec {
@@ -232,8 +233,12 @@ __global__ void __launch_bounds__(256)
       }
     }
     // V > 1 only when dim 0 has unit stride on both sides (checked by the planner)
-    *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) =
-        *reinterpret_cast<Vec const *>(in + oi + i0 * V * p.sin[0]);
+    if (ZERO) {
+      *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) = Vec{};
+    } else {
+      *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) =
+          *reinterpret_cast<Vec const *>(in + oi + i0 * V * p.sin[0]);
+    }
   }
 }
 
@@ -341,26 +346,32 @@ cudaError_t launch_cpx_expand(int esize, PermuteParams const &p, int64_t cpx_str
   return cudaErrorInvalidValue;
 }
 
+template <typename T, bool ZERO>
+static cudaError_t launch_copy_t(PermuteParams const &p, T const *i, T *o, int64_t blocks, cudaStream_t st) {
+  switch (p.vec) {
+    case 1: return launch_kernel(permute_copy_kernel<T, 1, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    case 2: return launch_kernel(permute_copy_kernel<T, 2, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    case 4: return launch_kernel(permute_copy_kernel<T, 4, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    case 8: return launch_kernel(permute_copy_kernel<T, 8, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    default: return cudaErrorInvalidValue;
+  }
+}
+
 template <typename T>
 static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void *out, int num_sms,
-                                    cudaStream_t st) {
+                                    bool zero, cudaStream_t st) {
   if (p.total == 0) return cudaSuccess;
   const T *i = static_cast<T const *>(in);
   T *o = static_cast<T *>(out);
   cudaError_t e = cudaSuccess;
+  if (zero && p.mode != 0) return cudaErrorInvalidValue;  // ZERO plans are row plans
   if (p.mode == 0) {
     int64_t work = p.total / p.vec;
     int64_t blocks = (work + 255) / 256;
     int64_t cap = (int64_t)num_sms * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    switch (p.vec) {
-      case 1: e = launch_kernel(permute_copy_kernel<T, 1>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
-      case 2: e = launch_kernel(permute_copy_kernel<T, 2>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
-      case 4: e = launch_kernel(permute_copy_kernel<T, 4>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
-      case 8: e = launch_kernel(permute_copy_kernel<T, 8>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o); break;
-      default: return cudaErrorInvalidValue;
-    }
+    e = zero ? launch_copy_t<T, true>(p, i, o, blocks, st) : launch_copy_t<T, false>(p, i, o, blocks, st);
   } else {
     int64_t nblk = ((p.size[0] + 31) / 32) * ((p.size[p.tdim_in] + 31) / 32) * p.batch;
     int64_t cap = (int64_t)num_sms * 8;  // 8 x 256 threads fill an SM: the copy is latency bound
@@ -377,11 +388,11 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
 }
 
 cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,
-                           int num_sms, cudaStream_t st) {
+                           int num_sms, cudaStream_t st, bool zero) {
   switch (esize) {
-    case 2: return launch_permute_t<uint16_t>(p, in, out, num_sms, st);
-    case 4: return launch_permute_t<uint32_t>(p, in, out, num_sms, st);
-    case 8: return launch_permute_t<uint64_t>(p, in, out, num_sms, st);
+    case 2: return launch_permute_t<uint16_t>(p, in, out, num_sms, zero, st);
+    case 4: return launch_permute_t<uint32_t>(p, in, out, num_sms, zero, st);
+    case 8: return launch_permute_t<uint64_t>(p, in, out, num_sms, zero, st);
     default: return cudaErrorInvalidValue;
   }
 }

@@ -144,6 +144,14 @@ int     eir_permute_plan_create(int32_t num_dims, int64_t const *sizes,
                                 int64_t const *strides_in, int64_t const *strides_out,
                                 int32_t dtype, eir_plan **plan);
 int     eir_permute(eir_plan *plan, void const *in, void *out, void *stream);
+/* unary plan with the reference's kernel type: EIR_KTYPE_COPY (= the permute
+ * above) or EIR_KTYPE_ZERO (out = 0 over strides_out; strides_in unused and
+ * eir_permute's `in` may be NULL). Replaces basic::UnaryBackend::init +
+ * compile with ktype_main COPY / ZERO (src/basic/unary/UnaryBackend.h:83-116,
+ * eval :125). */
+int     eir_unary_plan_create(int32_t num_dims, int64_t const *sizes,
+                              int64_t const *strides_in, int64_t const *strides_out,
+                              int32_t dtype, int32_t ktype, eir_plan **plan);
 
 /* --- plans -------------------------------------------------------------- */
 int     eir_plan_destroy(eir_plan *plan);

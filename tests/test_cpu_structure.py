@@ -20,9 +20,12 @@ REFLIB = ROOT / "oracle" / "_ref" / "libref_struct.so"
 
 
 def _header_functions():
-    txt = (ROOT / "include" / "eir_cuda.h").read_text()
-    txt = re.sub(r"/\*.*?\*/", "", txt, flags=re.S)
-    return sorted(set(re.findall(r"\b(eir_[a-z0-9_]+)\s*\(", txt)))
+    """every function declared by the C-ABI headers under include/"""
+    names = set()
+    for h in sorted((ROOT / "include").glob("*.h")):
+        txt = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names |= set(re.findall(r"\b(eir_[a-z0-9_]+)\s*\(", txt))
+    return sorted(names)
 
 
 def test_host_unit_tests():
