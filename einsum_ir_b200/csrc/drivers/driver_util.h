@@ -10,6 +10,7 @@
 #include <cstdint>
 #include <cstdio>
 #include <cstdlib>
+#include <algorithm>
 #include <cstring>
 #include <functional>
 #include <random>
@@ -105,7 +106,12 @@ inline std::vector<double> download(DeviceTensor const &t) {
 
 // Runs `fn` once to warm up, then enough repetitions for ~0.5 s (at least
 // `min_reps`), timed with CUDA events on `st`. Returns seconds per call.
+// Mean seconds per call of `fn` on `st`: one warm-up, one probe, then enough
+// calls for about EIR_DRIVER_TIME_MS milliseconds (default 500), at least
+// min_reps.
 inline double time_calls(std::function<void()> const &fn, cudaStream_t st, int min_reps = 10) {
+  double budget_ms = 500.0;
+  if (char const *v = std::getenv("EIR_DRIVER_TIME_MS")) budget_ms = std::max(1.0, std::atof(v));
   fn();
   check_cuda(cudaStreamSynchronize(st), "warm-up");
   cudaEvent_t e0, e1;
@@ -117,7 +123,7 @@ inline double time_calls(std::function<void()> const &fn, cudaStream_t st, int m
   check_cuda(cudaEventSynchronize(e1), "probe run");
   float ms = 0;
   cudaEventElapsedTime(&ms, e0, e1);
-  int64_t reps = (int64_t)(500.0 / (ms > 1e-3 ? ms : 1e-3));
+  int64_t reps = (int64_t)(budget_ms / (ms > 1e-3 ? ms : 1e-3));
   if (reps < min_reps) reps = min_reps;
   if (reps > 100000) reps = 100000;
   cudaEventRecord(e0, st);

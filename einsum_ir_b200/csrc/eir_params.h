@@ -66,6 +66,11 @@ struct TcParams {
   int32_t m_tiles, n_tiles, kp_blocks, k_steps;
   int32_t n_loops;
   int32_t group_m;                          // M tiles per raster group
+  // ring stages per accumulation chunk (0 = the whole K walk in one chunk):
+  // the tensor core's FP32 accumulation is biased over long K (about 2e-8
+  // relative per accumulating MMA), so long K walks accumulate chunk by chunk
+  // in TMEM and the epilogue adds the chunks in FP32 with rounding
+  int32_t k_chunk;
   int32_t first_touch, last_touch;
   int8_t a_src[5];
   int8_t b_src[5];

@@ -51,6 +51,7 @@ __device__ __forceinline__ void decompose(GroupDims const &g, int64_t x, int64_t
 }
 
 constexpr int kSimtBM = 64, kSimtBN = 64, kSimtBK = 16;
+constexpr int kSimtChunkK = 256;  // K per accumulation chunk (a multiple of kSimtBK)
 
 template <typename TL, typename TR, typename TO, typename TA>
 __global__ void __launch_bounds__(256)
@@ -94,11 +95,14 @@ __global__ void __launch_bounds__(256)
     col_a[t] = oa;
   }
 
-  TA acc[4][4];
+  // acc: the current chunk of kSimtChunkK products; tot: the sum of the
+  // chunks. Chunked accumulation keeps the rounding error of long K near
+  // (sqrt(chunk) + sqrt(K / chunk)) ulp instead of sqrt(K) ulp.
+  TA acc[4][4], tot[4][4];
 #pragma unroll
   for (int i = 0; i < 4; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = TA(0);
+    for (int j = 0; j < 4; ++j) acc[i][j] = tot[i][j] = TA(0);
 
   for (int64_t k0 = 0; k0 < K; k0 += BK) {
     if (tid < BK) {
@@ -151,7 +155,20 @@ __global__ void __launch_bounds__(256)
         for (int j = 0; j < 4; ++j) acc[i][j] += a[i] * b[j];
     }
     __syncthreads();
+    if (((k0 + BK) % kSimtChunkK) == 0) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          tot[i][j] += acc[i][j];
+          acc[i][j] = TA(0);
+        }
+    }
   }
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) tot[i][j] += acc[i][j];
 
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -165,7 +182,7 @@ __global__ void __launch_bounds__(256)
       if (n >= N) continue;
       const int64_t o = row_o[mm] + col_o[nn];
       const int64_t a = row_a[mm] + col_a[nn];
-      TA x = acc[i][j];
+      TA x = tot[i][j];
       if (p.first_touch == 3 /*COPY*/) x += static_cast<TA>(AUX[a]);
       else if (p.first_touch == 2 /*ADD*/) x += static_cast<TA>(OUT[o]) + static_cast<TA>(AUX[a]);
       else if (p.first_touch != 0 /*ZERO*/) x += static_cast<TA>(OUT[o]);

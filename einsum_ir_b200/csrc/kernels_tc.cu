@@ -184,15 +184,18 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
       int acc = 0;
       uint32_t acc_phase = 0;
       bool ok = true;
+      const int kc = p.k_chunk > 0 ? p.k_chunk : n_kstages;  // stages per accumulation chunk
       for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
+        const int rot = k_rotation(t, n_kstages);
+        for (int js0 = 0; js0 < n_kstages && ok; js0 += kc) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        const int rot = k_rotation(t, n_kstages);
-        for (int js = 0; js < n_kstages; ++js) {
+        const int js1 = min(js0 + kc, n_kstages);
+        for (int js = js0; js < js1; ++js) {
           int ksg = js + rot;
           if (ksg >= n_kstages) ksg -= n_kstages;
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
@@ -213,7 +216,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
                 const uint32_t b_off = B_MN ? kk * Cfg::kMmaK * 128 : kk * Cfg::kMmaK * Cfg::kEsize;
                 const uint64_t adesc = make_smem_desc(a_base + a_off, a_lbo, a_sbo, a_lay);
                 const uint64_t bdesc = make_smem_desc(b_base + b_off, b_lbo, b_sbo, b_lay);
-                const uint32_t accum = (js > 0 || sub > 0 || kk > 0) ? 1u : 0u;
+                const uint32_t accum = (js > js0 || sub > 0 || kk > 0) ? 1u : 0u;
                 if (KIND == kKindBF16) {
                   umma_f16(d_tmem, adesc, bdesc, idesc, accum);
                 } else if (KIND == kKindTF32) {
@@ -240,6 +243,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         umma_commit(&tfull[acc]);
         acc ^= 1;
         if (acc == 0) acc_phase ^= 1u;
+        }
       }
       if (!ok) {
         if (!*abort_flag) record_error(p.err, kErrTimeoutMma);
@@ -252,14 +256,21 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
     const int row = q * 32 + lane;
     int acc = 0;
     uint32_t acc_phase = 0;
-    for (int64_t t = blockIdx.x; t < p.total_tiles; t += gridDim.x) {
+    const int kc = p.k_chunk > 0 ? p.k_chunk : n_kstages;
+    const int n_chunks = (n_kstages + kc - 1) / kc;
+    bool ok = true;
+    for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
       TileCoord c = decode_tile(p, t);
+      for (int chunk = 0; chunk < n_chunks; ++chunk) {
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
         if (!*abort_flag) record_error(p.err, kErrTimeoutEpilogue);
         *abort_flag = 1;
+        ok = false;
         break;
       }
       tc_fence_after();
+      // -1: the whole K in one chunk; else first (0) / middle (1) / last (2)
+      const int part = n_chunks == 1 ? -1 : (chunk == 0 ? 0 : (chunk + 1 == n_chunks ? 2 : 1));
       const int64_t m = c.mt * BM + row;
       const bool mval = m < p.m_size;
       int64_t ob = m * p.so_m, ab = m * p.sa_m;
@@ -278,13 +289,17 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         tmem_ld_wait();
         if (!mval) continue;
         const int64_t nb = n0 + ch * 32;
-        store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
+        if (part < 0)
+          store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
+        else
+          store_chunk_part(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, part);
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (acc == 0) acc_phase ^= 1u;
+      }
     }
   } else if (Cfg::kSplit) {
     // ------------------------------------------------------------ hi/lo split

@@ -166,6 +166,46 @@ __device__ __forceinline__ int epilogue_kind(TcParams const &p) {
        : (p.first_touch == 3 && (p.last_touch == 99 || p.last_touch == 1)) ? 1 : 2;
 }
 
+// One accumulation chunk of a long K walk (TcParams::k_chunk), 32 columns of
+// one output row. part 0: the first chunk, with the plan's first touch;
+// part 1: a middle chunk, added to the partial sum stored by the previous
+// chunk; part 2: the last chunk, added, then the last touch. The partial sums
+// live in the output itself: the same thread wrote them, so they are visible.
+__device__ __forceinline__ void store_chunk_part(TcParams const &p, uint32_t const (&v)[32], float *op,
+                                                 const float *ap, int64_t nb, int64_t so_n, int64_t sa_n,
+                                                 int part) {
+  const int64_t rem = p.n_size - nb;
+  const int lim = rem < 32 ? (int)rem : 32;
+  if (part == 1 && lim == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      *op = __uint_as_float(v[j]) + *op;
+      op += so_n;
+    }
+    return;
+  }
+#pragma unroll
+  for (int j = 0; j < 32; ++j) {
+    if (j < lim) {
+      float x = __uint_as_float(v[j]);
+      if (part == 0) {
+        if (p.first_touch == 3 /*COPY*/) x += *ap;
+        else if (p.first_touch == 2 /*ADD*/) x += *op + *ap;
+        else if (p.first_touch != 0 /*not ZERO*/) x += *op;
+      } else {
+        x += *op;
+      }
+      if (part == 2) {
+        if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
+        else if (p.last_touch == 2 /*ADD*/) x += *ap;
+      }
+      *op = x;
+      op += so_n;
+      ap += sa_n;
+    }
+  }
+}
+
 // Writes 32 consecutive accumulator columns (output columns nb .. nb+31) of one
 // output row with the fused first / last touch. `op` / `ap` point at column nb
 // of the output / aux row; the full-chunk fast paths walk them by increments.

@@ -167,6 +167,30 @@ def test_tc_pair_shapes(cuda, expr, sizes, dtype, bn, ksub):
     assert "pair" in d and f"BN={bn} KSUB={ksub}" in d, d
 
 
+# Long K: the accumulation runs in chunks (512 K for FP32-exact, 2048 K for
+# TF32, 4096 K for BF16) that the epilogue adds in FP32; a single TMEM
+# accumulation over these K would drift past 1e-5 (about 2e-8 per MMA).
+LONG_K_CASES = [
+    ("mk,nk->nm", dict(m=128, n=256, k=16384), "fp32"),
+    ("km,kn->nm", dict(m=200, n=136, k=3000), "fp32"),           # ragged, partial last chunk
+    ("mkx,nkx->nm", dict(m=256, n=128, k=96, x=64), "fp32"),     # K = primitive x outer loop
+    ("mk,nk->nm", dict(m=128, n=256, k=20000), "tf32"),
+    ("mk,nk->nm", dict(m=128, n=256, k=32768), "bf16"),
+]
+LONG_K_TOUCH = [(cabi.KTYPE_ZERO, cabi.KTYPE_UNDEFINED, None),
+                (cabi.KTYPE_UNDEFINED, cabi.KTYPE_RELU, None),      # accumulate into out
+                (cabi.KTYPE_COPY, cabi.KTYPE_RELU, "m"),            # bias along n
+                (cabi.KTYPE_ADD, cabi.KTYPE_ADD, "n")]
+
+
+@pytest.mark.parametrize("pair", [0, 1])
+@pytest.mark.parametrize("first,last,aux", LONG_K_TOUCH)
+@pytest.mark.parametrize("expr,sizes,dtype", LONG_K_CASES)
+def test_tc_long_k_chunks(cuda, expr, sizes, dtype, first, last, aux, pair):
+    run_case(cuda, expr, sizes, dtype, first=first, last=last, aux_outer=aux, expect_family=TC,
+             pair=pair)
+
+
 def test_tc_tf32_general_inputs(cuda):
     run_case(cuda, "km,nk->nm", dict(m=256, n=256, k=256), "tf32", tf32_general=True,
              expect_family=TC)
@@ -229,6 +253,13 @@ SIMT_CASES = [
 @pytest.mark.parametrize("expr,sizes,dtype", SIMT_CASES)
 def test_simt_parity(cuda, expr, sizes, dtype):
     run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT)
+
+
+def test_simt_long_k(cuda):
+    """K = 65536 on the CUDA cores: chunked FP32 accumulation keeps the error
+    near 2e-6 (a single FP32 running sum drifts to ~1.5e-5)"""
+    run_case(cuda, "mk,nk->nm", dict(m=64, n=96, k=65536), "fp32", flags=cabi.FLAG_FORCE_SIMT,
+             expect_family=SIMT)
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "fp64"])
