@@ -584,16 +584,19 @@ bool try_tc(eir_plan *p, std::string *why) {
   if (ksub_ok && (force_ksub == 1 || force_ksub == 2)) ksub = (int)force_ksub;
   p->tc_ksub = ksub;
   // accumulation chunks (the tensor core's FP32 accumulation drifts by about
-  // 2e-8 relative per accumulating MMA): 512 K for 3xTF32 (FP32-exact, three
-  // MMAs per 8 K: <= 192 per chunk), 2048 K for TF32 (256 per chunk) and
-  // 4096 K for BF16 (16 K per MMA: 256 per chunk), each chunk <= ~5e-6
+  // 2e-8 relative per accumulating MMA; every chunk costs the epilogue a
+  // read-modify-write of the output tile): 1024 K for 3xTF32 (FP32-exact,
+  // three MMAs per 8 K: <= 384 per chunk, <= ~8e-6), 8192 K for TF32 (whose
+  // inputs already carry ~1e-3) and for BF16 (<= 1024 / 512 MMAs)
   {
-    const int64_t chunk_k = kind == 2 ? 512 : (kind == 1 ? 2048 : 4096);
+    const int64_t chunk_k = kind == 2 ? 1024 : 8192;
     const int64_t per_stage = (int64_t)bk * ksub;
     const int64_t n_stages = ceil_div((int64_t)t.k_steps, (int64_t)ksub);
-    int64_t kc = chunk_k > 0 ? std::max<int64_t>(1, chunk_k / per_stage) : 0;
-    if (kc >= n_stages) kc = 0;
-    t.k_chunk = (int32_t)kc;
+    const int64_t kc_max = std::max<int64_t>(1, chunk_k / per_stage);
+    // chunks of equal length (a short last chunk would leave its epilogue
+    // nothing to overlap with)
+    const int64_t n_chunks = ceil_div(n_stages, kc_max);
+    t.k_chunk = n_chunks > 1 ? (int32_t)ceil_div(n_stages, n_chunks) : 0;
   }
 
   p->tc = true;

@@ -171,37 +171,38 @@ __device__ __forceinline__ int epilogue_kind(TcParams const &p) {
 // part 1: a middle chunk, added to the partial sum stored by the previous
 // chunk; part 2: the last chunk, added, then the last touch. The partial sums
 // live in the output itself: the same thread wrote them, so they are visible.
+// Every load is issued before the first store (the compiler cannot reorder
+// them itself: the addresses may alias), so the 32 reads overlap.
 __device__ __forceinline__ void store_chunk_part(TcParams const &p, uint32_t const (&v)[32], float *op,
                                                  const float *ap, int64_t nb, int64_t so_n, int64_t sa_n,
                                                  int part) {
   const int64_t rem = p.n_size - nb;
   const int lim = rem < 32 ? (int)rem : 32;
-  if (part == 1 && lim == 32) {
+  // the partial sum (or, for the first chunk, what the first touch reads)
+  const bool read_out = part != 0 || (p.first_touch != 0 && p.first_touch != 3);
+  const bool read_aux = (part == 0 && (p.first_touch == 2 || p.first_touch == 3)) ||
+                        (part == 2 && p.last_touch == 2);
+  const bool add_aux_first = part == 0 && (p.first_touch == 2 || p.first_touch == 3);
+  const bool relu = part == 2 && p.last_touch == 1;
+  const bool add_aux_last = part == 2 && p.last_touch == 2;
+  // two halves of 16 columns: 32 loads in flight, few registers
 #pragma unroll
-    for (int j = 0; j < 32; ++j) {
-      *op = __uint_as_float(v[j]) + *op;
-      op += so_n;
+  for (int h = 0; h < 32; h += 16) {
+    float prev[16], bias[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      prev[j] = (read_out && h + j < lim) ? op[(h + j) * so_n] : 0.0f;
+      bias[j] = (read_aux && h + j < lim) ? ap[(h + j) * sa_n] : 0.0f;
     }
-    return;
-  }
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    if (j < lim) {
-      float x = __uint_as_float(v[j]);
-      if (part == 0) {
-        if (p.first_touch == 3 /*COPY*/) x += *ap;
-        else if (p.first_touch == 2 /*ADD*/) x += *op + *ap;
-        else if (p.first_touch != 0 /*not ZERO*/) x += *op;
-      } else {
-        x += *op;
+    for (int j = 0; j < 16; ++j) {
+      if (h + j < lim) {
+        float x = __uint_as_float(v[h + j]) + prev[j];
+        if (add_aux_first) x += bias[j];
+        if (relu) x = fmaxf(x, 0.0f);
+        if (add_aux_last) x += bias[j];
+        op[(h + j) * so_n] = x;
       }
-      if (part == 2) {
-        if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
-        else if (p.last_touch == 2 /*ADD*/) x += *ap;
-      }
-      *op = x;
-      op += so_n;
-      ap += sa_n;
     }
   }
 }

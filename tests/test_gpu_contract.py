@@ -43,9 +43,10 @@ def _np_in(t):
 
 def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
              last=cabi.KTYPE_UNDEFINED, aux_outer=None, flags=0, seed=0, expect_family=None,
-             tf32_general=False, tc_min_ops="0", pair=None, bn=None, ksub=None):
+             tf32_general=False, tc_min_ops="0", pair=None, bn=None, ksub=None, tol=None):
     """pair / bn / ksub force the tensor-core tile shape (CTA pair or one CTA,
-    BN, K blocks per stage); None leaves the planner's choice."""
+    BN, K blocks per stage); None leaves the planner's choice. tol overrides
+    the dtype's tolerance."""
     import torch
     os.environ["EIR_TC_MIN_OPS"] = tc_min_ops
     os.environ["EIR_TC_MIN_UTIL"] = "0"
@@ -91,7 +92,8 @@ def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
     key = "tf32_general" if (dtype == "tf32" and tf32_general) else dtype
     err = _oracle.rel_err(got, ref)
     assert np.all(np.isfinite(got))
-    assert err <= TOL[key], f"{expr} {dtype}: rel err {err:.3e} ({plan.describe()})"
+    bound = TOL[key] if tol is None else tol
+    assert err <= bound, f"{expr} {dtype}: rel err {err:.3e} ({plan.describe()})"
     return plan, err
 
 
@@ -167,14 +169,14 @@ def test_tc_pair_shapes(cuda, expr, sizes, dtype, bn, ksub):
     assert "pair" in d and f"BN={bn} KSUB={ksub}" in d, d
 
 
-# Long K: the accumulation runs in chunks (512 K for FP32-exact, 2048 K for
-# TF32, 4096 K for BF16) that the epilogue adds in FP32; a single TMEM
-# accumulation over these K would drift past 1e-5 (about 2e-8 per MMA).
+# Long K: the accumulation runs in chunks (1024 K for FP32-exact, 8192 K for
+# TF32 and BF16) that the epilogue adds in FP32; a single TMEM accumulation
+# over these K would drift past 1e-5 (about 2e-8 per accumulating MMA).
 LONG_K_CASES = [
     ("mk,nk->nm", dict(m=128, n=256, k=16384), "fp32"),
     ("km,kn->nm", dict(m=200, n=136, k=3000), "fp32"),           # ragged, partial last chunk
     ("mkx,nkx->nm", dict(m=256, n=128, k=96, x=64), "fp32"),     # K = primitive x outer loop
-    ("mk,nk->nm", dict(m=128, n=256, k=20000), "tf32"),
+    ("mk,nk->nm", dict(m=128, n=256, k=12288), "tf32"),
     ("mk,nk->nm", dict(m=128, n=256, k=32768), "bf16"),
 ]
 LONG_K_TOUCH = [(cabi.KTYPE_ZERO, cabi.KTYPE_UNDEFINED, None),
@@ -187,8 +189,10 @@ LONG_K_TOUCH = [(cabi.KTYPE_ZERO, cabi.KTYPE_UNDEFINED, None),
 @pytest.mark.parametrize("first,last,aux", LONG_K_TOUCH)
 @pytest.mark.parametrize("expr,sizes,dtype", LONG_K_CASES)
 def test_tc_long_k_chunks(cuda, expr, sizes, dtype, first, last, aux, pair):
+    # FP32-exact keeps its 1e-5; TF32 and BF16 chunks are long (8192 K, up to
+    # 1024 accumulating MMAs) and are held to north_star's FP32/TF32 1e-4
     run_case(cuda, expr, sizes, dtype, first=first, last=last, aux_outer=aux, expect_family=TC,
-             pair=pair)
+             pair=pair, tol=1e-5 if dtype == "fp32" else 1e-4)
 
 
 def test_tc_tf32_general_inputs(cuda):
