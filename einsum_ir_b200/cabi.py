@@ -33,6 +33,8 @@ EXPORTS = [
     "eir_expression_tensor_dims", "eir_expression_destroy", "eir_expression_describe",
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
     "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc", "eir_unary_plan_create",
+    "eir_contract_peers", "eir_ipc_get_handle", "eir_ipc_open_handle", "eir_ipc_close_handle",
+    "eir_copy_to_peers",
     # include/eir_tensor_operation.h
     "eir_top_create", "eir_top_destroy", "eir_top_setup", "eir_top_execute", "eir_top_plan",
     "eir_top_default_optimization_config", "eir_top_optimize",
@@ -72,6 +74,11 @@ def lib() -> ctypes.CDLL:
         L.eir_contract_plan_create.argtypes = [POINTER(EirContractDesc), POINTER(c_void_p)]
         L.eir_contract.argtypes = [c_void_p] * 6
         L.eir_contract_no_alloc.argtypes = [c_void_p] * 6
+        L.eir_contract_peers.argtypes = [c_void_p] * 5 + [c_int32, POINTER(c_void_p), c_void_p]
+        L.eir_ipc_get_handle.argtypes = [c_void_p, c_void_p, POINTER(c_int64)]
+        L.eir_ipc_open_handle.argtypes = [c_void_p, c_int64, POINTER(c_void_p), POINTER(c_void_p)]
+        L.eir_ipc_close_handle.argtypes = [c_void_p]
+        L.eir_copy_to_peers.argtypes = [c_void_p, c_int32, POINTER(c_void_p), c_int64, c_void_p]
         L.eir_contract_num_ops.argtypes = [c_void_p]
         L.eir_contract_num_ops.restype = c_int64
         L.eir_permute_plan_create.argtypes = [c_int32, POINTER(c_int64), POINTER(c_int64),
@@ -216,6 +223,43 @@ class ContractPlan(Plan):
         """eir_contract_no_alloc: same result, scratch from the library's static array."""
         check(lib().eir_contract_no_alloc(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
                                           c_void_p(stream)))
+
+    def contract_peers(self, left, right, out, peer_outs: Sequence, aux=None, stream: int = 0) -> None:
+        """eir_contract_peers: out and every peer output (device pointers or
+        tensors with out's layout) receive the result."""
+        ptrs = [_ptr(p) for p in peer_outs]
+        arr = (c_void_p * max(1, len(ptrs)))(*ptrs)
+        check(lib().eir_contract_peers(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
+                                       len(ptrs), arr, c_void_p(stream)))
+
+
+IPC_HANDLE_BYTES = 64
+
+
+def ipc_get_handle(dev_ptr) -> tuple:
+    """(handle bytes, offset) of a device pointer for another process of the node"""
+    h = ctypes.create_string_buffer(IPC_HANDLE_BYTES)
+    off = c_int64()
+    check(lib().eir_ipc_get_handle(_ptr(dev_ptr), h, ctypes.byref(off)))
+    return bytes(h.raw), int(off.value)
+
+
+def ipc_open_handle(handle: bytes, offset: int) -> tuple:
+    """(device pointer, mapping base) of another process's buffer"""
+    ptr, base = c_void_p(), c_void_p()
+    check(lib().eir_ipc_open_handle(ctypes.create_string_buffer(handle, IPC_HANDLE_BYTES), offset,
+                                    ctypes.byref(ptr), ctypes.byref(base)))
+    return int(ptr.value), int(base.value)
+
+
+def ipc_close_handle(base: int) -> None:
+    check(lib().eir_ipc_close_handle(c_void_p(base)))
+
+
+def copy_to_peers(src, dsts: Sequence, nbytes: int, stream: int = 0) -> None:
+    """copy-engine copies of nbytes from src to every destination pointer"""
+    arr = (c_void_p * max(1, len(dsts)))(*[_ptr(d) for d in dsts])
+    check(lib().eir_copy_to_peers(_ptr(src), len(dsts), arr, int(nbytes), c_void_p(stream)))
 
 
 class PermutePlan(Plan):

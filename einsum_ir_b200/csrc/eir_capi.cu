@@ -679,9 +679,11 @@ struct ProfScope {
 };
 
 int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
-             cudaStream_t st) {
+             eir::PeerOutputs const *peers, cudaStream_t st) {
   ProfScope prof(p, st);
-  cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt, l, r, aux, out, st);
+  eir::SimtParams sp = p->simt;
+  if (peers != nullptr) sp.peers = *peers;
+  cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, sp, l, r, aux, out, st);
   if (e != cudaSuccess) return cuda_fail(e, "simt contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;
@@ -902,7 +904,13 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   return EIR_SUCCESS;
 }
 
-int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, void *out, void *stream) {
+}  // extern "C"
+
+namespace {
+
+// eir_contract, with optional peer copies of the output (eir_contract_peers)
+int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+                  eir::PeerOutputs const *peers, void *stream) {
   if (p == nullptr || p->what != 1) return set_error(EIR_INVALID_ARGUMENT, "not a contraction plan");
   if (p->empty) return EIR_SUCCESS;
   if (l == nullptr || r == nullptr || out == nullptr)
@@ -930,16 +938,17 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
                                            ds->num_sms, st);
     if (e != cudaSuccess) return cuda_fail(e, "complex expansion launch");
     g_launches.fetch_add(1, std::memory_order_relaxed);
-    return eir_contract(p->cpx_inner, l, p->ws, aux, out, stream);
+    return contract_impl(p->cpx_inner, l, p->ws, aux, out, peers, stream);
   }
-  if (p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA) return run_simt(p, l, r, aux, out, st);
+  if (p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA)
+    return run_simt(p, l, r, aux, out, peers, st);
 
   DeviceState *ds = nullptr;
   int rc = device_state(&ds);
   if (rc != EIR_SUCCESS) return rc;
   // TMA needs 16-byte aligned bases; otherwise take the generic path
   if ((reinterpret_cast<uintptr_t>(l) & 15) || (reinterpret_cast<uintptr_t>(r) & 15))
-    return run_simt(p, l, r, aux, out, st);
+    return run_simt(p, l, r, aux, out, peers, st);
 
   void const *a_ptr = l, *b_ptr = r;
   if (p->prepack >= 0) {
@@ -984,10 +993,104 @@ int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, voi
   }
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
+  if (peers != nullptr) tp.peers = *peers;
   ProfScope prof(p, st);
   cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, ds->num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
+
+// base address of the device allocation holding `ptr` (driver API through
+// the runtime's entry-point query, as for the tensor-map encoder)
+typedef CUresult (*PfnMemGetAddressRange)(CUdeviceptr *, size_t *, CUdeviceptr);
+int allocation_base(void const *ptr, char **base) {
+  static PfnMemGetAddressRange fn = nullptr;
+  if (fn == nullptr) {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfnMemGetAddressRange>(f);
+  }
+  if (fn == nullptr) return set_error(EIR_CUDA_ERROR, "cuMemGetAddressRange unavailable");
+  CUdeviceptr b = 0;
+  size_t size = 0;
+  CUresult r = fn(&b, &size, reinterpret_cast<CUdeviceptr>(ptr));
+  if (r != CUDA_SUCCESS) return set_error(EIR_CUDA_ERROR, "cuMemGetAddressRange failed (" + std::to_string((int)r) + ")");
+  *base = reinterpret_cast<char *>(b);
+  return EIR_SUCCESS;
+}
+
+}  // namespace
+
+extern "C" {
+
+int eir_contract(eir_plan *p, void const *l, void const *r, void const *aux, void *out, void *stream) {
+  return contract_impl(p, l, r, aux, out, nullptr, stream);
+}
+
+int eir_contract_peers(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+                       int32_t num_peers, void *const *peer_outs, void *stream) {
+  if (num_peers < 0 || num_peers > eir::kMaxPeers)
+    return set_error(EIR_INVALID_ARGUMENT, "num_peers must be 0.." + std::to_string(eir::kMaxPeers));
+  if (num_peers > 0 && peer_outs == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null peer list");
+  if (p != nullptr && p->what == 1 && p->cpx_inner != nullptr && num_peers > 0)
+    return set_error(EIR_INVALID_ARGUMENT, "peer outputs are not supported for complex plans");
+  eir::PeerOutputs peers;
+  peers.n = num_peers;
+  for (int i = 0; i < num_peers; ++i) {
+    if (peer_outs[i] == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null peer output");
+    peers.ptr[i] = peer_outs[i];
+  }
+  return contract_impl(p, l, r, aux, out, num_peers > 0 ? &peers : nullptr, stream);
+}
+
+int eir_copy_to_peers(void const *src, int32_t num_peers, void *const *dsts, int64_t bytes, void *stream) {
+  if (bytes < 0 || num_peers < 0 || (num_peers > 0 && (src == nullptr || dsts == nullptr)))
+    return set_error(EIR_INVALID_ARGUMENT, "bad argument");
+  for (int i = 0; i < num_peers; ++i) {
+    if (dsts[i] == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null peer destination");
+    // one copy per destination; the copy engines move it, no SM is used
+    cudaError_t e = cudaMemcpyAsync(dsts[i], src, (size_t)bytes, cudaMemcpyDeviceToDevice,
+                                    static_cast<cudaStream_t>(stream));
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(peer)");
+  }
+  return EIR_SUCCESS;
+}
+
+int eir_ipc_get_handle(void const *dev_ptr, void *handle, int64_t *offset) {
+  if (dev_ptr == nullptr || handle == nullptr || offset == nullptr)
+    return set_error(EIR_INVALID_ARGUMENT, "null argument");
+  char *base = nullptr;
+  int rc = allocation_base(dev_ptr, &base);
+  if (rc != EIR_SUCCESS) return rc;
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcGetMemHandle");
+  static_assert(sizeof(h) == EIR_IPC_HANDLE_BYTES, "IPC handle size");
+  std::memcpy(handle, &h, sizeof(h));
+  *offset = static_cast<char const *>(dev_ptr) - base;
+  return EIR_SUCCESS;
+}
+
+int eir_ipc_open_handle(void const *handle, int64_t offset, void **dev_ptr, void **base) {
+  if (handle == nullptr || dev_ptr == nullptr || base == nullptr || offset < 0)
+    return set_error(EIR_INVALID_ARGUMENT, "bad argument");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle, sizeof(h));
+  void *b = nullptr;
+  cudaError_t e = cudaIpcOpenMemHandle(&b, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcOpenMemHandle");
+  *base = b;
+  *dev_ptr = static_cast<char *>(b) + offset;
+  return EIR_SUCCESS;
+}
+
+int eir_ipc_close_handle(void *base) {
+  if (base == nullptr) return EIR_SUCCESS;
+  cudaError_t e = cudaIpcCloseMemHandle(base);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaIpcCloseMemHandle");
   return EIR_SUCCESS;
 }
 

@@ -21,6 +21,18 @@ struct GroupDims {
   int64_t sa[kMaxGroupDims] = {};   // out_aux strides
 };
 
+constexpr int kMaxPeers = 7;
+
+// Copies of the output on other GPUs (peer memory mapped into this process):
+// the epilogue stores every final output element to `out` and, at the same
+// element offset, to each peer output (an all-gather fused into the
+// contraction; the stores cross NVLink while the next tiles compute).
+struct PeerOutputs {
+  int32_t n = 0;
+  int32_t pad_ = 0;
+  void *ptr[kMaxPeers] = {};
+};
+
 struct SimtParams {
   GroupDims c, m, n, k;
   int32_t first_touch;  // EIR_KTYPE_*
@@ -28,6 +40,7 @@ struct SimtParams {
   int32_t a_kfast;      // left: K is the fast (stride-1) direction -> load along K
   int32_t b_kfast;      // right: K is the fast direction
   int64_t m_tiles, n_tiles;
+  PeerOutputs peers;
 };
 
 // Permute: dims sorted so that dim 0 is the output's fastest dim.
@@ -76,6 +89,7 @@ struct TcParams {
   int8_t b_src[5];
   int16_t pad_;
   uint32_t *err;                            // device error word
+  PeerOutputs peers;
 };
 
 }  // namespace eir

@@ -246,6 +246,7 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
               if (p.last_touch == 1 /*RELU*/) x = x > 0.0 ? x : 0.0;
               else if (p.last_touch == 2 /*ADD*/) x += aux[a];
               out[o] = x;
+              for (int q = 0; q < p.peers.n; ++q) static_cast<double *>(p.peers.ptr[q])[o] = x;
             }
           }
         }

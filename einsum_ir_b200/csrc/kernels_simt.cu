@@ -189,6 +189,7 @@ __global__ void __launch_bounds__(256)
       if (p.last_touch == 1 /*RELU*/) x = x > TA(0) ? x : TA(0);
       else if (p.last_touch == 2 /*ADD*/) x += static_cast<TA>(AUX[a]);
       OUT[o] = static_cast<TO>(x);
+      for (int q = 0; q < p.peers.n; ++q) static_cast<TO *>(p.peers.ptr[q])[o] = static_cast<TO>(x);
     }
   }
 }

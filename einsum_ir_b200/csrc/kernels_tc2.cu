@@ -333,6 +333,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
           store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
         else
           store_chunk_part(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, part);
+        if (p.peers.n > 0 && part != 0 && part != 1)  // final values only
+          copy_to_peers(p, out + ob + nb * so_n, ob + nb * so_n, nb, so_n);
       }
       tc_fence_before();
       __syncwarp();

@@ -207,6 +207,48 @@ __device__ __forceinline__ void store_chunk_part(TcParams const &p, uint32_t con
   }
 }
 
+// Copies the (up to) 32 final output values of one row chunk, just stored at
+// `op` = out + off by this thread, to every peer output at the same offset.
+__device__ __forceinline__ void copy_to_peers(TcParams const &p, float const *op, int64_t off, int64_t nb,
+                                              int64_t so_n) {
+  const int64_t rem = p.n_size - nb;
+  const int lim = rem < 32 ? (int)rem : 32;
+  if (so_n == 1 && lim == 32 && ((reinterpret_cast<uintptr_t>(op) & 15) == 0)) {
+    // the row's 32 values are contiguous: 16-byte vectors (a warp's lanes
+    // hold different rows, so 4-byte stores would each be a separate write
+    // over NVLink)
+    float4 x[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) x[j] = reinterpret_cast<float4 const *>(op)[j];
+    for (int i = 0; i < p.peers.n; ++i) {
+      float4 *dst = reinterpret_cast<float4 *>(static_cast<float *>(p.peers.ptr[i]) + off);
+      if (reinterpret_cast<uintptr_t>(dst) & 15) {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          float *d = reinterpret_cast<float *>(dst) + 4 * j;
+          d[0] = x[j].x;
+          d[1] = x[j].y;
+          d[2] = x[j].z;
+          d[3] = x[j].w;
+        }
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) dst[j] = x[j];
+      }
+    }
+    return;
+  }
+  float x[32];
+#pragma unroll
+  for (int j = 0; j < 32; ++j) x[j] = j < lim ? op[j * so_n] : 0.0f;
+  for (int i = 0; i < p.peers.n; ++i) {
+    float *dst = static_cast<float *>(p.peers.ptr[i]) + off;
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < lim) dst[j * so_n] = x[j];
+  }
+}
+
 // Writes 32 consecutive accumulator columns (output columns nb .. nb+31) of one
 // output row with the fused first / last touch. `op` / `ap` point at column nb
 // of the output / aux row; the full-chunk fast paths walk them by increments.

@@ -138,6 +138,36 @@ int64_t eir_contract_num_ops(eir_plan const *plan);
 int     eir_contract_no_alloc(eir_plan *plan, void const *left, void const *right,
                               void const *out_aux, void *out, void *stream);
 
+/* Same contraction as eir_contract, and every final output element is also
+ * stored, at the same element offset, into each of num_peers (<= 7) other
+ * output buffers: typically the outputs of the other GPUs of a batch-sharded
+ * contraction, mapped into this process with eir_ipc_open_handle, so that
+ * the all-gather of the output happens inside the contraction's epilogue
+ * (plain stores over NVLink, overlapped with the next tiles) instead of a
+ * separate collective. The peer buffers must have out's layout and extent.
+ * Their contents are complete when the call's kernels have completed; a
+ * reader on another GPU synchronises with this stream first (e.g. a
+ * cross-process barrier after a stream synchronisation). Not for complex
+ * plans. No counterpart in the reference (it has no multi-GPU path). */
+int     eir_contract_peers(eir_plan *plan, void const *left, void const *right,
+                           void const *out_aux, void *out, int32_t num_peers,
+                           void *const *peer_outs, void *stream);
+
+/* CUDA IPC of device buffers between the processes of one node (one process
+ * per GPU): a handle (EIR_IPC_HANDLE_BYTES opaque bytes) and offset for a
+ * pointer into any cudaMalloc'd allocation; the opening process gets the
+ * pointer (mapped with peer access) and the mapping's base for closing. */
+enum { EIR_IPC_HANDLE_BYTES = 64 };
+/* copies `bytes` from src to each of num_peers destinations (typically peer
+ * buffers mapped with eir_ipc_open_handle), one asynchronous copy-engine copy
+ * per destination on `stream`: the gather step of a sharded contraction
+ * that overlaps the next block's kernels without taking SMs from them */
+int     eir_copy_to_peers(void const *src, int32_t num_peers, void *const *dsts, int64_t bytes,
+                          void *stream);
+int     eir_ipc_get_handle(void const *dev_ptr, void *handle, int64_t *offset);
+int     eir_ipc_open_handle(void const *handle, int64_t offset, void **dev_ptr, void **base);
+int     eir_ipc_close_handle(void *base);
+
 /* --- unary permute (copy with reordered strides) ------------------------- */
 /* sizes/strides are per dimension, in elements; any order */
 int     eir_permute_plan_create(int32_t num_dims, int64_t const *sizes,
