@@ -448,7 +448,15 @@ bool try_tc(eir_plan *p, std::string *why) {
   if (device_state(&ds) == EIR_SUCCESS) num_sms = ds->num_sms;
   int bn = 128;
   bool pair = false;
-  if (kind != 3) {
+  // Split-K: when one-CTA 128 x 128 tiles would fill under half the SMs and
+  // the K walk is long, the K walk is split into slices that run as separate
+  // work items (one-CTA kernel; partial tiles reduced by a second kernel)
+  int64_t k_blocks_total = ceil_div(d[kp].size, (int64_t)bk);
+  for (int i : ko) k_blocks_total *= d[i].size;
+  const int64_t tiles_128 = ceil_div(d[mp].size, 128) * ceil_div(d[np].size, 128) * loop_tiles;
+  const bool split_k = kind != 3 && env_int("EIR_TC_SPLITK", 1) != 0 && tiles_128 * 2 <= num_sms &&
+                       k_blocks_total >= 64;
+  if (kind != 3 && !split_k) {
     const int64_t force_bn = env_int("EIR_TC_BN", 0);     // tuning override: 128 or 256
     const int64_t force_pair = env_int("EIR_TC_PAIR", -1);  // tuning override: 0 or 1
     double best = 0.0;
@@ -583,6 +591,21 @@ bool try_tc(eir_plan *p, std::string *why) {
   int64_t force_ksub = env_int("EIR_TC_KSUB", 0);  // tuning override: 1 or 2
   if (ksub_ok && (force_ksub == 1 || force_ksub == 2)) ksub = (int)force_ksub;
   p->tc_ksub = ksub;
+  // split-K slices: enough work items for the SMs, >= 8 stages per slice
+  t.base_tiles = t.total_tiles;
+  t.split_k = 1;
+  t.ws_slice = 0;
+  p->split_ws_offset = 0;
+  if (split_k) {
+    const int64_t n_st = ceil_div((int64_t)t.k_steps, (int64_t)ksub);
+    const int64_t s = std::min<int64_t>(std::min<int64_t>(num_sms / t.total_tiles, n_st / 8), 32);
+    const int64_t out_elems = t.m_size * t.n_size * loop_tiles;
+    if (s >= 2 && s * out_elems * 4 <= (int64_t(1) << 30)) {
+      t.split_k = (int32_t)s;
+      t.ws_slice = out_elems;
+      t.total_tiles *= s;
+    }
+  }
   // accumulation chunks (the tensor core's FP32 accumulation drifts by about
   // 2e-8 relative per accumulating MMA; every chunk costs the epilogue a
   // read-modify-write of the output tile): 1024 K for 3xTF32 (FP32-exact,
@@ -629,18 +652,22 @@ bool try_tc(eir_plan *p, std::string *why) {
     p->pre = pre;
     p->ws_bytes = bytes_of(left);
   }
+  if (t.split_k > 1) {
+    p->split_ws_offset = (p->ws_bytes + 255) / 256 * 256;
+    p->ws_bytes = p->split_ws_offset + (int64_t)t.split_k * t.ws_slice * 4;
+  }
 
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "tc kind=%s %sBN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
-                "tiles=%lld ksteps=%d prepack=%s",
+                "tiles=%lld ksteps=%d prepack=%s splitk=%d",
                 kind == 0 ? "bf16" : kind == 1 ? "tf32" : kind == 2 ? "3xtf32" : "fp64-dmma",
                 pair ? "pair BM=256 " : "", bn,
                 p->tc_ksub, a_mn ? "MN" : "K",
                 b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
                 (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
                 (long long)t.total_tiles, t.k_steps,
-                prepack < 0 ? "none" : (prepack == 0 ? "left" : "right"));
+                prepack < 0 ? "none" : (prepack == 0 ? "left" : "right"), (int)t.split_k);
   *why = buf;
   return true;
 }
@@ -697,6 +724,32 @@ int api_set_error(int code, char const *msg) { return set_error(code, msg); }
 int api_cuda_fail(cudaError_t e, char const *where) { return cuda_fail(e, where); }
 int api_encode_map(MapSpec const &s, void const *ptr, CUtensorMap *m) { return encode_map(s, ptr, m); }
 void api_count_launch() { g_launches.fetch_add(1, std::memory_order_relaxed); }
+int api_launch_tc_split(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
+                        TcParams const &tp, void const *aux, void *out, float *ws, int num_sms,
+                        cudaStream_t st) {
+  // the slices write dense partial tiles [slice][tile loops][n][m] with a
+  // ZERO first touch and no last touch; the reduction applies the plan's
+  TcParams ts = tp;
+  ts.first_touch = 0;
+  ts.last_touch = 99;
+  ts.so_m = 1;
+  ts.so_n = tp.m_size;
+  ts.sa_m = ts.sa_n = 0;
+  int64_t stride = tp.m_size * tp.n_size;
+  for (int i = 0; i < kMaxTileLoops; ++i) {
+    ts.loop_so[i] = stride;
+    ts.loop_sa[i] = 0;
+    if (i < tp.n_loops) stride *= tp.loop_size[i];
+  }
+  ts.peers = PeerOutputs();
+  cudaError_t e = api_launch_tc(p, ma, mb, ts, nullptr, ws, num_sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "tc split-K launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  e = launch_splitk_reduce(tp, ws, static_cast<float const *>(aux), static_cast<float *>(out), num_sms, st);
+  if (e != cudaSuccess) return cuda_fail(e, "split-K reduction launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
 cudaError_t api_launch_tc(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
                           TcParams const &tp, void const *aux, void *out, int num_sms,
                           cudaStream_t st) {
@@ -951,7 +1004,7 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
     return run_simt(p, l, r, aux, out, peers, st);
 
   void const *a_ptr = l, *b_ptr = r;
-  if (p->prepack >= 0) {
+  if (p->ws_bytes > 0) {  // pre-permuted operand and / or split-K partial tiles
     int dev = 0;
     cudaGetDevice(&dev);
     if (p->ws == nullptr || p->ws_device != dev) {
@@ -963,6 +1016,8 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
       }
       p->ws_device = dev;
     }
+  }
+  if (p->prepack >= 0) {
     void const *src = p->prepack == 0 ? l : r;
     rc = eir_permute(p->pre, src, p->ws, stream);
     if (rc != EIR_SUCCESS) return rc;
@@ -995,6 +1050,10 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
   tp.err = ds->err;
   if (peers != nullptr) tp.peers = *peers;
   ProfScope prof(p, st);
+  if (tp.split_k > 1) {
+    float *ws = reinterpret_cast<float *>(static_cast<char *>(p->ws) + p->split_ws_offset);
+    return eir::api_launch_tc_split(p, ma, mb, tp, aux, out, ws, ds->num_sms, st);
+  }
   cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, ds->num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);

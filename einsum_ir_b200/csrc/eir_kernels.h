@@ -10,6 +10,11 @@ namespace eir {
 cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const &p, void const *l,
                                  void const *r, void const *aux, void *out, cudaStream_t st);
 
+// split-K reduction of a split tcgen05 plan (TcParams::split_k): p is the
+// plan's real parameter block (output strides and touches), ws the workspace
+cudaError_t launch_splitk_reduce(TcParams const &p, float const *ws, float const *aux, float *out,
+                                 int num_sms, cudaStream_t st);
+
 // zero: the unary ZERO primitive (out = 0 over p's output strides, `in` unused;
 // p must be a row-copy plan, which planning with sin = sout gives)
 cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, void *out,

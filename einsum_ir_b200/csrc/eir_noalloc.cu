@@ -91,7 +91,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   if (p->cpx_inner != nullptr)
     return eir::api_set_error(EIR_INVALID_ARGUMENT,
                               "eir_contract_no_alloc: complex plans need their expansion workspace");
-  if (p->prepack >= 0 && (size_t)p->ws_bytes > kStaticOperandBytes) {
+  if ((size_t)p->ws_bytes > kStaticOperandBytes) {
     char buf[192];
     std::snprintf(buf, sizeof(buf),
                   "eir_contract_no_alloc: plan needs %lld bytes of scratch, the static scratch "
@@ -151,6 +151,10 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   }
   eir::TcParams tp = p->tcp;
   tp.err = reinterpret_cast<uint32_t *>(d->scratch);  // header word
+  if (tp.split_k > 1) {  // split-K partial tiles after the pre-permuted operand, as in eir_contract
+    float *ws = reinterpret_cast<float *>(d->scratch + kStaticHeaderBytes + p->split_ws_offset);
+    return eir::api_launch_tc_split(p, ma, mb, tp, aux, out, ws, d->num_sms, st);
+  }
   cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, d->num_sms, st);
   if (e != cudaSuccess) return eir::api_cuda_fail(e, "tc contraction launch");
   eir::api_count_launch();

@@ -84,6 +84,13 @@ struct TcParams {
   // relative per accumulating MMA), so long K walks accumulate chunk by chunk
   // in TMEM and the epilogue adds the chunks in FP32 with rounding
   int32_t k_chunk;
+  // split-K (one-CTA kernel): work item t is slice t / base_tiles of tile
+  // t % base_tiles; slice s covers K stages [s n / split_k, (s+1) n / split_k)
+  // and writes its partial tile into a dense FP32 workspace (out + s *
+  // ws_slice), which a reduction kernel sums into the output
+  int32_t split_k;
+  int64_t base_tiles;
+  int64_t ws_slice;
   int32_t first_touch, last_touch;
   int8_t a_src[5];
   int8_t b_src[5];

@@ -48,6 +48,11 @@ namespace eir {
 cudaError_t api_launch_tc(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
                           TcParams const &tp, void const *aux, void *out, int num_sms,
                           cudaStream_t st);
+// a split-K plan (TcParams::split_k > 1): slices into the workspace `ws`,
+// then the reduction into `out` with the plan's touches and peers
+int api_launch_tc_split(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
+                        TcParams const &tp, void const *aux, void *out, float *ws, int num_sms,
+                        cudaStream_t st);
 }  // namespace eir
 
 struct eir_plan {
@@ -82,6 +87,7 @@ struct eir_plan {
   eir_plan *pre = nullptr;
   void *ws = nullptr;
   int64_t ws_bytes = 0;
+  int64_t split_ws_offset = 0;  // split-K partial tiles: ws + this offset
   int ws_device = -1;
 
   // ---- permute (unary COPY) or unary ZERO

@@ -147,10 +147,12 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           }
         };
         KWalk kw = pt.kw;
-        const int rot = pt.rot;
-        for (int js = 0; js < n_kstages; ++js) {
+        const int rot = pt.rot, kbeg = pt.kbeg, klen = pt.klen;
+        for (int js = 0; js < klen; ++js) {
           int ksg = js + rot;
-          if (ksg >= n_kstages) ksg -= n_kstages;
+          if (ksg >= klen) ksg -= klen;
+          if (rot > 0 && js == klen - rot) kw.seek(p, kbeg * KSUB);  // wrap to the item's first stage
+          ksg += kbeg;
           if (!mbar_wait_bounded(&empty[stage], phase ^ 1u, abort_flag)) {
             if (!*abort_flag) record_error(p.err, kErrTimeoutProducer);
             *abort_flag = 1;
@@ -186,18 +188,20 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
       bool ok = true;
       const int kc = p.k_chunk > 0 ? p.k_chunk : n_kstages;  // stages per accumulation chunk
       for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-        const int rot = k_rotation(t, n_kstages);
-        for (int js0 = 0; js0 < n_kstages && ok; js0 += kc) {
+        const KRange kr = tile_krange(p, t, n_kstages);
+        const int rot = k_rotation(t, kr.len);
+        for (int js0 = 0; js0 < kr.len && ok; js0 += kc) {
         if (!mbar_wait_bounded(&tempty[acc], acc_phase ^ 1u, abort_flag)) {
           ok = false;
           break;
         }
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + (uint32_t)(acc * BN);
-        const int js1 = min(js0 + kc, n_kstages);
+        const int js1 = min(js0 + kc, kr.len);
         for (int js = js0; js < js1; ++js) {
           int ksg = js + rot;
-          if (ksg >= n_kstages) ksg -= n_kstages;
+          if (ksg >= kr.len) ksg -= kr.len;
+          ksg += kr.begin;
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
           uint64_t *ready = Cfg::kSplit ? &conv[stage] : &full[stage];
           if (!mbar_wait_bounded(ready, phase, abort_flag)) {
@@ -257,10 +261,13 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
     int acc = 0;
     uint32_t acc_phase = 0;
     const int kc = p.k_chunk > 0 ? p.k_chunk : n_kstages;
-    const int n_chunks = (n_kstages + kc - 1) / kc;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
       TileCoord c = decode_tile(p, t);
+      const int n_chunks = (tile_krange(p, t, n_kstages).len + kc - 1) / kc;
+      // split-K: this slice's partial tile goes to its workspace slice
+      float *const tout =
+          out + (p.split_k > 1 ? (int64_t)((uint32_t)t / (uint32_t)p.base_tiles) * p.ws_slice : 0);
       for (int chunk = 0; chunk < n_chunks; ++chunk) {
       if (!mbar_wait_warp(&tfull[acc], acc_phase, abort_flag)) {
         if (!*abort_flag) record_error(p.err, kErrTimeoutEpilogue);
@@ -290,11 +297,11 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
         if (!mval) continue;
         const int64_t nb = n0 + ch * 32;
         if (part < 0)
-          store_chunk(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
+          store_chunk(p, v, tout + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, fast);
         else
-          store_chunk_part(p, v, out + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, part);
+          store_chunk_part(p, v, tout + ob + nb * so_n, aux + ab + nb * sa_n, nb, so_n, sa_n, part);
         if (p.peers.n > 0 && part != 0 && part != 1)  // final values only
-          copy_to_peers(p, out + ob + nb * so_n, ob + nb * so_n, nb, so_n);
+          copy_to_peers(p, tout + ob + nb * so_n, ob + nb * so_n, nb, so_n);
       }
       tc_fence_before();
       __syncwarp();
@@ -310,7 +317,8 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
     uint32_t phase = 0;
     bool ok = true;
     for (int64_t t = blockIdx.x; t < p.total_tiles && ok; t += gridDim.x) {
-      for (int js = 0; js < n_kstages; ++js) {
+      const int klen = tile_krange(p, t, n_kstages).len;
+      for (int js = 0; js < klen; ++js) {
         if (!mbar_wait_bounded(&full[stage], phase, abort_flag)) {
           ok = false;
           break;
@@ -401,5 +409,50 @@ cudaError_t launch_tc_contract(int kind, int bn, int ksub, bool a_mn, bool b_mn,
 }
 
 int tc_block_k(int kind) { return kind == kKindBF16 ? 64 : (kind == 3 ? 16 : 32); }
+
+// Split-K reduction: out = last_touch(first_touch(out, aux) + sum over s of
+// ws[s]) for the dense workspace [slice][tile loops][n][m] of a split plan,
+// summed in slice order (deterministic); peer copies as in the epilogues.
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const TcParams p, const float *__restrict__ ws, const float *__restrict__ aux,
+                         float *__restrict__ out) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t M = p.m_size, N = p.n_size, total = p.ws_slice;
+  for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < total;
+       e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t m = e % M, r = e / M;
+    const int64_t n = r % N;
+    int64_t l = r / N;
+    int64_t o = m * p.so_m + n * p.so_n, a = m * p.sa_m + n * p.sa_n;
+#pragma unroll
+    for (int i = 0; i < kMaxTileLoops; ++i) {
+      if (i < p.n_loops) {
+        const int64_t li = l % p.loop_size[i];
+        l /= p.loop_size[i];
+        o += li * p.loop_so[i];
+        a += li * p.loop_sa[i];
+      }
+    }
+    float x = 0.0f;
+    for (int s = 0; s < p.split_k; ++s) x += ws[(int64_t)s * total + e];
+    if (p.first_touch == 3 /*COPY*/) x += aux[a];
+    else if (p.first_touch == 2 /*ADD*/) x += out[o] + aux[a];
+    else if (p.first_touch != 0 /*not ZERO*/) x += out[o];
+    if (p.last_touch == 1 /*RELU*/) x = fmaxf(x, 0.0f);
+    else if (p.last_touch == 2 /*ADD*/) x += aux[a];
+    out[o] = x;
+    for (int q = 0; q < p.peers.n; ++q) static_cast<float *>(p.peers.ptr[q])[o] = x;
+  }
+}
+
+cudaError_t launch_splitk_reduce(TcParams const &p, float const *ws, float const *aux, float *out,
+                                 int num_sms, cudaStream_t st) {
+  int64_t blocks = (p.ws_slice + 255) / 256;
+  const int64_t cap = (int64_t)num_sms * 8;
+  if (blocks > cap) blocks = cap;
+  if (blocks < 1) blocks = 1;
+  return launch_kernel(splitk_reduce_kernel, dim3((unsigned)blocks), dim3(256), 0, st, p, ws, aux, out);
+}
 
 }  // namespace eir

@@ -27,7 +27,7 @@ struct TileCoord {
 // group_m M tiles. 32-bit arithmetic: the planner keeps tile counts below 2^31.
 __device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t tile) {
   TileCoord c;
-  uint32_t t = (uint32_t)tile;
+  uint32_t t = (uint32_t)tile % (uint32_t)p.base_tiles;  // the output tile of a split-K slice
   const uint32_t mn = (uint32_t)p.m_tiles * (uint32_t)p.n_tiles;
   const uint32_t u = t % mn;
   t /= mn;
@@ -112,6 +112,20 @@ struct KWalk {
   }
 };
 
+// K stages [begin, begin + len) of work item t (all of K without split-K)
+struct KRange {
+  int begin, len;
+};
+__device__ __forceinline__ KRange tile_krange(TcParams const &p, int64_t t, int n_kstages) {
+  KRange r{0, n_kstages};
+  if (p.split_k > 1) {
+    const int s = (int)((uint32_t)t / (uint32_t)p.base_tiles);
+    r.begin = (int)((int64_t)s * n_kstages / p.split_k);
+    r.len = (int)((int64_t)(s + 1) * n_kstages / p.split_k) - r.begin;
+  }
+  return r;
+}
+
 // Start offset (in stages) of a tile's K walk. Tiles running at the same time
 // start at different K positions so they do not all fetch the same operand
 // lines at once (the sum over K is order independent up to FP32 rounding).
@@ -127,6 +141,7 @@ __device__ __forceinline__ int k_rotation(int64_t t, int n_stages) {
 struct ProducerTile {
   TileCoord c;
   int rot, mrow, nrow;
+  int kbeg, klen;  // the work item's K stages (tile_krange)
   SlotCoords sa, sb;
   KWalk kw;
 };
@@ -138,12 +153,15 @@ __device__ __forceinline__ ProducerTile producer_tile(TcParams const &p, int64_t
                                                       int m_rows, int m_off, int n_cols, int n_off) {
   ProducerTile pt;
   pt.c = decode_tile(p, t);
-  pt.rot = k_rotation(t, n_kstages);
+  const KRange kr = tile_krange(p, t, n_kstages);
+  pt.kbeg = kr.begin;
+  pt.klen = kr.len;
+  pt.rot = k_rotation(t, kr.len);
   pt.mrow = pt.c.mt * m_rows + m_off;
   pt.nrow = pt.c.nt * n_cols + n_off;
   pt.sa = slot_coords(p.a_src, pt.c);
   pt.sb = slot_coords(p.b_src, pt.c);
-  pt.kw.seek(p, pt.rot * KSUB);
+  pt.kw.seek(p, (kr.begin + pt.rot) * KSUB);
   return pt;
 }
 

@@ -195,6 +195,26 @@ def test_tc_long_k_chunks(cuda, expr, sizes, dtype, first, last, aux, pair):
              pair=pair, tol=1e-5 if dtype == "fp32" else 1e-4)
 
 
+# Split-K: few output tiles and a long K walk run as K slices (one-CTA
+# kernel, partial tiles in a workspace) summed by a reduction kernel, which
+# applies the touch kernels.
+SPLITK_CASES = [
+    ("mk,nk->nm", dict(m=128, n=128, k=16384), "fp32"),
+    ("km,kn->nm", dict(m=200, n=136, k=8192), "bf16"),
+    ("cmk,cnk->cnm", dict(c=2, m=128, n=96, k=6000), "tf32"),     # tile loop, ragged K
+    ("mkx,nkx->nm", dict(m=96, n=128, k=64, x=96), "fp32"),       # K = primitive x outer loop
+]
+
+
+@pytest.mark.parametrize("first,last,aux", LONG_K_TOUCH)
+@pytest.mark.parametrize("expr,sizes,dtype", SPLITK_CASES)
+def test_tc_split_k(cuda, expr, sizes, dtype, first, last, aux):
+    plan, _ = run_case(cuda, expr, sizes, dtype, first=first, last=last, aux_outer=aux,
+                       expect_family=TC, tol=1e-4 if dtype == "tf32" else 1e-5)
+    d = plan.describe()
+    assert "splitk=" in d and "splitk=1 " not in d and "pair" not in d, d
+
+
 def test_tc_tf32_general_inputs(cuda):
     run_case(cuda, "km,nk->nm", dict(m=256, n=256, k=256), "tf32", tf32_general=True,
              expect_family=TC)

@@ -23,6 +23,7 @@ CASES = [
     ("zcdef,zabcd->zabef", dict(z=2, a=8, b=8, c=8, d=8, e=16, f=16), "fp64", cabi.FAMILY_DMMA, 0),
     ("mk,nk->nm", dict(m=70, n=50, k=40), "fp32", cabi.FAMILY_SIMT, cabi.FLAG_FORCE_SIMT),
     ("akmj,njk->anm", dict(a=2, k=4, m=128, j=64, n=256), "bf16", cabi.FAMILY_TC, 0),  # pre-permute
+    ("mk,nk->nm", dict(m=128, n=128, k=16384), "fp32", cabi.FAMILY_TC, 0),  # split-K: the reduction stores
 ]
 
 

@@ -46,6 +46,23 @@ def test_no_alloc_matches_contract(cuda, monkeypatch):
         assert err <= TOL, f"call {call}: rel err {err:.3e}"
 
 
+def test_no_alloc_split_k(cuda, monkeypatch):
+    """a split-K plan: partial tiles in the static scratch, then the reduction"""
+    import torch
+    monkeypatch.setenv("EIR_TC_MIN_OPS", "0")
+    plan, (sl, sr, so) = _plan("mk,nk->nm", dict(m=128, n=128, k=16384))
+    assert "splitk=1 " not in plan.describe() and plan.workspace_bytes > 0, plan.describe()
+    g = torch.Generator().manual_seed(12)
+    l = ((torch.rand(sl, generator=g) * 2 - 1).to(torch.bfloat16)).to(cuda)
+    r = ((torch.rand(sr, generator=g) * 2 - 1).to(torch.bfloat16)).to(cuda)
+    want = torch.full(so, float("nan"), device=cuda)
+    got = torch.full(so, float("nan"), device=cuda)
+    plan.contract(l, r, want)
+    plan.contract_no_alloc(l, r, got)
+    torch.cuda.synchronize()
+    assert torch.equal(got, want)  # same kernels, same slices, same summation order
+
+
 def test_no_alloc_rejects_oversized_scratch(cuda):
     import torch
     # the pre-permuted (smaller) operand is the right one: 512*64*256 BF16 = 16 MiB,
