@@ -705,89 +705,8 @@ struct ProfScope {
   }
 };
 
-// CUDA-core operand re-layout: when an operand has a unit-stride dim that the
-// kernel's load order does not use (the kernel walks the output-fastest M / N
-// dim, or the operand's fastest K dim), every load of it touches its own
-// 32-byte sector. Copy such an operand (>= 8 MB) once, with the permute
-// kernels, into a packed layout whose fastest dims are the kernel's M (or N)
-// group order, then K, then C; the group strides point into the copy.
-void plan_simt_prepack(eir_plan *p, std::string *why) {
-  int64_t off = 0;
-  for (int side = 0; side < 2; ++side) {
-    const bool left = side == 0;
-    eir::GroupDims *own = left ? &p->simt.m : &p->simt.n;
-    const int64_t esize = dtype_bytes(left ? p->dt_l : p->dt_r);
-    auto stride = [&](eir::GroupDims const &g, int i) { return left ? g.sl[i] : g.sr[i]; };
-    // the stride the kernel's consecutive threads walk
-    const bool kfast = left ? p->simt.a_kfast : p->simt.b_kfast;
-    const int64_t walked = kfast ? (p->simt.k.n ? std::llabs(stride(p->simt.k, 0)) : 0)
-                                 : (own->n ? std::llabs(stride(*own, 0)) : 0);
-    int64_t unit = INT64_MAX, elems = 1;
-    for (eir::GroupDims const *g : {&p->simt.c, own, &p->simt.k})
-      for (int i = 0; i < g->n; ++i) {
-        unit = std::min<int64_t>(unit, std::llabs(stride(*g, i)));
-        elems *= g->size[i];
-      }
-    if (walked == 1 || unit != 1 || elems * esize < (int64_t(8) << 20) || own->n == 0) continue;
-    // packed layout: own group (kernel order), then K, then C
-    std::vector<int64_t> sizes, from, to;
-    int64_t s = 1;
-    for (eir::GroupDims *g : {own, &p->simt.k, &p->simt.c})
-      for (int i = 0; i < g->n; ++i) {
-        sizes.push_back(g->size[i]);
-        from.push_back(stride(*g, i));
-        to.push_back(s);
-        (left ? g->sl[i] : g->sr[i]) = s;
-        s *= g->size[i];
-      }
-    eir_plan *pre = nullptr;
-    if (eir_permute_plan_create((int32_t)sizes.size(), sizes.data(), from.data(), to.data(),
-                                left ? p->dt_l : p->dt_r, &pre) != EIR_SUCCESS) {
-      // keep the operand's own strides
-      eir::SimtParams const &d = p->simt_direct;
-      if (left) {
-        std::copy(d.m.sl, d.m.sl + eir::kMaxGroupDims, p->simt.m.sl);
-        std::copy(d.k.sl, d.k.sl + eir::kMaxGroupDims, p->simt.k.sl);
-        std::copy(d.c.sl, d.c.sl + eir::kMaxGroupDims, p->simt.c.sl);
-      } else {
-        std::copy(d.n.sr, d.n.sr + eir::kMaxGroupDims, p->simt.n.sr);
-        std::copy(d.k.sr, d.k.sr + eir::kMaxGroupDims, p->simt.k.sr);
-        std::copy(d.c.sr, d.c.sr + eir::kMaxGroupDims, p->simt.c.sr);
-      }
-      continue;
-    }
-    p->simt_pre[side] = pre;
-    p->simt_pre_off[side] = off;
-    off += (s * esize + 255) / 256 * 256;
-    if (left) p->simt.a_kfast = 0;
-    else p->simt.b_kfast = 0;
-    *why += left ? "; left re-laid out" : "; right re-laid out";
-  }
-  if (off > 0) p->ws_bytes = off;
-}
-
 int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
              eir::PeerOutputs const *peers, cudaStream_t st) {
-  if (p->simt_pre[0] != nullptr || p->simt_pre[1] != nullptr) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    if (p->ws == nullptr || p->ws_device != dev) {
-      if (p->ws != nullptr) cudaFree(p->ws);
-      cudaError_t e = cudaMalloc(&p->ws, (size_t)p->ws_bytes);
-      if (e != cudaSuccess) {
-        p->ws = nullptr;
-        return cuda_fail(e, "cudaMalloc(workspace)");
-      }
-      p->ws_device = dev;
-    }
-    for (int side = 0; side < 2; ++side) {
-      if (p->simt_pre[side] == nullptr) continue;
-      void *dst = static_cast<char *>(p->ws) + p->simt_pre_off[side];
-      int rc = eir_permute(p->simt_pre[side], side == 0 ? l : r, dst, st);
-      if (rc != EIR_SUCCESS) return rc;
-      (side == 0 ? l : r) = dst;
-    }
-  }
   ProfScope prof(p, st);
   eir::SimtParams sp = p->simt;
   if (peers != nullptr) sp.peers = *peers;
@@ -1021,13 +940,11 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   p->simt.m_tiles = ceil_div(p->simt.m.total, 64);
   p->simt.n_tiles = ceil_div(p->simt.n.total, 64);
 
-  p->simt_direct = p->simt;
   std::string why = "forced";
   if (!p->empty && !(desc->flags & EIR_FLAG_FORCE_SIMT) && try_tc(p, &why)) {
     p->family = p->tc_kind == 3 ? EIR_FAMILY_DMMA : EIR_FAMILY_TC;
   } else {
     p->family = EIR_FAMILY_SIMT;
-    if (!p->empty && !(desc->flags & EIR_FLAG_NO_PREPACK)) plan_simt_prepack(p, &why);
   }
   std::string dims_txt;
   for (auto const &x : p->dims) {
@@ -1323,8 +1240,6 @@ int eir_plan_destroy(eir_plan *p) {
     cudaEventDestroy(ev.second);
   }
   if (p->pre) eir_plan_destroy(p->pre);
-  for (eir_plan *q : p->simt_pre)
-    if (q) eir_plan_destroy(q);
   if (p->cpx_inner) eir_plan_destroy(p->cpx_inner);
   if (p->ws) {
     int cur = 0;

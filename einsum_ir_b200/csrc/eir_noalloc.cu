@@ -91,10 +91,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
   if (p->cpx_inner != nullptr)
     return eir::api_set_error(EIR_INVALID_ARGUMENT,
                               "eir_contract_no_alloc: complex plans need their expansion workspace");
-  // scratch used here: a tensor-core plan's pre-permuted operand and split-K
-  // partial tiles (a CUDA-core plan reads its operands in place here)
-  const bool tc_plan = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
-  if (tc_plan && (size_t)p->ws_bytes > kStaticOperandBytes) {
+  if ((size_t)p->ws_bytes > kStaticOperandBytes) {
     char buf[192];
     std::snprintf(buf, sizeof(buf),
                   "eir_contract_no_alloc: plan needs %lld bytes of scratch, the static scratch "
@@ -109,8 +106,7 @@ extern "C" int eir_contract_no_alloc(eir_plan *p, void const *l, void const *r, 
 
   const bool aligned = !((reinterpret_cast<uintptr_t>(l) | reinterpret_cast<uintptr_t>(r)) & 15);
   if ((p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA) || !aligned) {
-    // the operands' own strides: no workspace for a CUDA-core re-layout here
-    cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt_direct, l, r, aux, out, st);
+    cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, p->simt, l, r, aux, out, st);
     if (e != cudaSuccess) return eir::api_cuda_fail(e, "simt contraction launch");
     eir::api_count_launch();
     return EIR_SUCCESS;

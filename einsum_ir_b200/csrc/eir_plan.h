@@ -85,12 +85,6 @@ struct eir_plan {
   // operand pre-permute into the plan's workspace (0 = left, 1 = right, -1 = none)
   int prepack = -1;
   eir_plan *pre = nullptr;
-  // CUDA-core plans: operands re-laid out so that the kernel's fastest M / N
-  // index is contiguous (0 left, 1 right); simt holds the packed strides,
-  // simt_direct the operands' own (for entry points without a workspace)
-  eir_plan *simt_pre[2] = {nullptr, nullptr};
-  int64_t simt_pre_off[2] = {0, 0};
-  eir::SimtParams simt_direct;
   void *ws = nullptr;
   int64_t ws_bytes = 0;
   int64_t split_ws_offset = 0;  // split-K partial tiles: ws + this offset

@@ -279,16 +279,6 @@ def test_simt_parity(cuda, expr, sizes, dtype):
     run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT)
 
 
-@pytest.mark.parametrize("expr", ["fbad,cf->bcda", "cf,fbad->bcda"])
-@pytest.mark.parametrize("first,last,aux", LONG_K_TOUCH)
-def test_simt_operand_relayout(cuda, expr, first, last, aux):
-    """an operand (>= 8 MB) whose unit-stride dim is not the one the CUDA-core
-    kernel walks is re-laid out once into the workspace (left, then right)"""
-    plan, _ = run_case(cuda, expr, dict(a=64, b=32, c=24, d=32, f=36), "fp32", first=first, last=last,
-                       aux_outer=aux, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT)
-    assert "re-laid out" in plan.describe() and plan.workspace_bytes > 0, plan.describe()
-
-
 def test_simt_long_k(cuda):
     """K = 65536 on the CUDA cores: chunked FP32 accumulation keeps the error
     near 2e-6 (a single FP32 running sum drifts to ~1.5e-5)"""

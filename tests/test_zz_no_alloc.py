@@ -63,28 +63,6 @@ def test_no_alloc_split_k(cuda, monkeypatch):
     assert torch.equal(got, want)  # same kernels, same slices, same summation order
 
 
-def test_no_alloc_simt_relayout(cuda, monkeypatch):
-    """a CUDA-core plan with an operand re-layout: the no-allocation entry point
-    reads the operand in place (same products and K order, same result)"""
-    import torch
-    il, ir, io, names = binary.parse_binary("fbad,cf->bcda")
-    sizes = dict(a=64, b=32, c=24, d=32, f=36)
-    sz = {i: sizes[c] for i, c in enumerate(names)}
-    dims = binary.contraction_dims(il, ir, io, sz)
-    plan = cabi.ContractPlan(dims, cabi.FP32, cabi.FP32, cabi.FP32, 0, cabi.KTYPE_ZERO, cabi.KTYPE_MADD,
-                             cabi.KTYPE_UNDEFINED, cabi.FLAG_FORCE_SIMT)
-    assert "re-laid out" in plan.describe(), plan.describe()
-    g = torch.Generator().manual_seed(13)
-    l = (torch.rand([sz[i] for i in il], generator=g) * 2 - 1).to(cuda)
-    r = (torch.rand([sz[i] for i in ir], generator=g) * 2 - 1).to(cuda)
-    want = torch.full([sz[i] for i in io], float("nan"), device=cuda)
-    got = torch.full([sz[i] for i in io], float("nan"), device=cuda)
-    plan.contract(l, r, want)
-    plan.contract_no_alloc(l, r, got)
-    torch.cuda.synchronize()
-    assert torch.equal(got, want)
-
-
 def test_no_alloc_rejects_oversized_scratch(cuda):
     import torch
     # the pre-permuted (smaller) operand is the right one: 512*64*256 BF16 = 16 MiB,
