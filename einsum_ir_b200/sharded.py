@@ -175,13 +175,16 @@ class ShardedContraction:
             cabi.ipc_close_handle(b)
         self._peer_ptrs, self._peer_bases, self._bound = [], [], None
 
-    def run_ce(self, left, right, out, comm_stream=None) -> None:
+    def run_ce(self, left, right, out, comm_streams=None) -> None:
         """This rank's blocks, each computed into its final place in the local
         `out` and then copied by the copy engines into every other rank's
-        `out` (bind_output(out) first), on a side stream while the next block
-        computes: the gather takes no SM from the contraction kernel. The
-        output is complete on all ranks once every rank's stream has passed
-        this call (synchronise, then a cross-rank barrier, before reading)."""
+        `out` (bind_output(out) first) while the next block computes: the
+        gather takes no SM from the contraction kernel. The copy to each peer
+        runs on a stream of its own (`comm_streams`, one per peer), so the
+        copies of one block proceed in parallel on several copy engines
+        instead of one after another. The output is complete on all ranks
+        once every rank's stream has passed this call (synchronise, then a
+        cross-rank barrier, before reading)."""
         import torch
         if self._bound != out.data_ptr():
             raise RuntimeError("run_ce: bind_output(out) first")
@@ -189,7 +192,9 @@ class ShardedContraction:
             raise ValueError("run_ce: out must be contiguous")
         lay = self.layout
         compute = torch.cuda.current_stream()
-        comm = comm_stream or torch.cuda.Stream()
+        comm = list(comm_streams) if comm_streams else []
+        while len(comm) < len(self._peer_ptrs):
+            comm.append(torch.cuda.Stream())
         row_bytes = out[0].numel() * out.element_size()
         for start in lay.owned(self.rank):
             lsl = left[start:start + lay.block] if self.shard_dim in self.il else left
@@ -199,11 +204,12 @@ class ShardedContraction:
             if self._peer_ptrs:
                 ev = torch.cuda.Event()
                 ev.record(compute)
-                comm.wait_event(ev)
                 off = start * row_bytes
-                cabi.copy_to_peers(dst, [p + off for p in self._peer_ptrs], lay.block * row_bytes,
-                                   stream=comm.cuda_stream)
-        compute.wait_stream(comm)
+                for peer, st in zip(self._peer_ptrs, comm):
+                    st.wait_event(ev)
+                    cabi.copy_to_peers(dst, [peer + off], lay.block * row_bytes, stream=st.cuda_stream)
+        for st in comm[:len(self._peer_ptrs)]:
+            compute.wait_stream(st)
 
     def run_fused(self, left, right, out) -> None:
         """This rank's blocks, each stored by the epilogue into `out` of every
@@ -255,8 +261,9 @@ def _main() -> int:
         sc = ShardedContraction("zabcd,zcdef->zabef", sizes, dt, world, rank,
                                 chunks=4 if world < 8 else 2, dtype_comp=comp)
     comm = torch.cuda.Stream()
+    comm_streams = [torch.cuda.Stream() for _ in range(max(0, world - 1))]
     step = {"fused": lambda: sc.run_fused(left, right, out),
-            "ce": lambda: sc.run_ce(left, right, out, comm),
+            "ce": lambda: sc.run_ce(left, right, out, comm_streams),
             "nccl": lambda: sc.run(left, right, out, comm)}[mode]
     for _ in range(2):
         step()
