@@ -34,7 +34,7 @@ EXPORTS = [
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
     "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc", "eir_unary_plan_create",
     "eir_contract_peers", "eir_ipc_get_handle", "eir_ipc_open_handle", "eir_ipc_close_handle",
-    "eir_copy_to_peers",
+    "eir_copy_to_peers", "eir_contract_gather",
     # include/eir_tensor_operation.h
     "eir_top_create", "eir_top_destroy", "eir_top_setup", "eir_top_execute", "eir_top_plan",
     "eir_top_default_optimization_config", "eir_top_optimize",
@@ -75,6 +75,7 @@ def lib() -> ctypes.CDLL:
         L.eir_contract.argtypes = [c_void_p] * 6
         L.eir_contract_no_alloc.argtypes = [c_void_p] * 6
         L.eir_contract_peers.argtypes = [c_void_p] * 5 + [c_int32, POINTER(c_void_p), c_void_p]
+        L.eir_contract_gather.argtypes = [c_void_p] * 5 + [c_int32, POINTER(c_void_p), c_void_p]
         L.eir_ipc_get_handle.argtypes = [c_void_p, c_void_p, POINTER(c_int64)]
         L.eir_ipc_open_handle.argtypes = [c_void_p, c_int64, POINTER(c_void_p), POINTER(c_void_p)]
         L.eir_ipc_close_handle.argtypes = [c_void_p]
@@ -231,6 +232,15 @@ class ContractPlan(Plan):
         arr = (c_void_p * max(1, len(ptrs)))(*ptrs)
         check(lib().eir_contract_peers(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
                                        len(ptrs), arr, c_void_p(stream)))
+
+    def contract_gather(self, left, right, out, peer_outs: Sequence, aux=None, stream: int = 0) -> None:
+        """eir_contract_gather: the contraction, then copy-engine copies of
+        the output into every peer buffer (device pointers with out's extent),
+        slab by slab as the kernel finishes them where the plan allows."""
+        ptrs = [_ptr(p) for p in peer_outs]
+        arr = (c_void_p * max(1, len(ptrs)))(*ptrs)
+        check(lib().eir_contract_gather(self._h, _ptr(left), _ptr(right), _ptr(aux), _ptr(out),
+                                        len(ptrs), arr, c_void_p(stream)))
 
 
 IPC_HANDLE_BYTES = 64

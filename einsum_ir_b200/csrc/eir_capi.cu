@@ -430,6 +430,15 @@ bool try_tc(eir_plan *p, std::string *why) {
     *why = "more than two outer K dims";
     return false;
   }
+  // the tile loop with the largest output stride becomes the slowest one:
+  // tiles then finish slab by slab of the output's outermost dim, which
+  // eir_contract_gather moves to the peers one slab at a time
+  if (loops.size() > 1) {
+    auto outer = std::max_element(loops.begin(), loops.end(), [&](int a, int b) {
+      return std::llabs(d[a].so) < std::llabs(d[b].so);
+    });
+    std::rotate(outer, outer + 1, loops.end());
+  }
   if ((int)loops.size() > eir::kMaxTileLoops) {
     *why = "more than four tile-loop dims";
     return false;
@@ -677,6 +686,42 @@ bool valid_first(int k) {
 }
 bool valid_last(int k) {
   return k == EIR_KTYPE_RELU || k == EIR_KTYPE_ADD || k == EIR_KTYPE_UNDEFINED;
+}
+
+// Output layout facts for eir_contract_gather: whether the output is one
+// contiguous block, and its slabs along the outermost output dim when that
+// dim is the tensor-core kernel's slowest tile loop (tiles finish slab by slab).
+void plan_gather(eir_plan *p) {
+  std::vector<LDim> od;
+  for (auto const &x : p->dims)
+    if (x.type != EIR_DIM_K) od.push_back(x);
+  std::sort(od.begin(), od.end(), [](LDim const &a, LDim const &b) { return a.so < b.so; });
+  bool dense = true;
+  int64_t elems = 1;
+  for (auto const &x : od) {
+    if (x.so != elems) dense = false;
+    elems *= x.size;
+  }
+  p->out_dense = dense;
+  p->out_elems = elems;
+  p->slab_count = 1;
+  p->slab_elems = elems;
+  p->slab_loop = -1;
+  p->slab_counted = false;
+  p->slab_target = 1;
+  eir::TcParams const &t = p->tcp;
+  const bool tc = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
+  if (!dense || !tc || t.split_k > 1 || t.n_loops < 1 || od.empty()) return;
+  const int j = t.n_loops - 1;
+  if (t.loop_so[j] != od.back().so || t.loop_size[j] != od.back().size || t.loop_size[j] < 2) return;
+  p->slab_count = t.loop_size[j];
+  p->slab_elems = t.loop_so[j];
+  p->slab_loop = j;
+  if (p->family == EIR_FAMILY_DMMA) {
+    // every math warp of the DMMA kernel counts each tile it stores
+    p->slab_counted = true;
+    p->slab_target = (uint32_t)(t.total_tiles / p->slab_count) * 8u;
+  }
 }
 
 // events around a plan's main kernel when profiling is enabled
@@ -935,6 +980,7 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   }
   p->simt.first_touch = p->first;
   p->simt.last_touch = p->last;
+  p->simt.round_tf32 = (p->comp == EIR_COMPUTE_TF32 && dl == EIR_FP32 && dr == EIR_FP32) ? 1 : 0;
   p->simt.a_kfast = min_abs_stride(p->dims, EIR_DIM_K, true) < min_abs_stride(p->dims, EIR_DIM_M, true);
   p->simt.b_kfast = min_abs_stride(p->dims, EIR_DIM_K, false) < min_abs_stride(p->dims, EIR_DIM_N, false);
   p->simt.m_tiles = ceil_div(p->simt.m.total, 64);
@@ -946,6 +992,7 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   } else {
     p->family = EIR_FAMILY_SIMT;
   }
+  plan_gather(p);
   std::string dims_txt;
   for (auto const &x : p->dims) {
     dims_txt += type_name(x.type);
@@ -953,6 +1000,9 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   }
   const bool tensor_cores = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
   p->text = (tensor_cores ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
+  if (p->out_dense)
+    p->text += "| gather: " + std::to_string(p->slab_count) + " slab(s)" +
+               (p->slab_counted ? ", counted by the kernel" : ", released after the kernel");
   *plan_out = p;
   return EIR_SUCCESS;
 }
@@ -963,7 +1013,7 @@ namespace {
 
 // eir_contract, with optional peer copies of the output (eir_contract_peers)
 int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
-                  eir::PeerOutputs const *peers, void *stream) {
+                  eir::PeerOutputs const *peers, void *stream, uint32_t *slab_ctr = nullptr) {
   if (p == nullptr || p->what != 1) return set_error(EIR_INVALID_ARGUMENT, "not a contraction plan");
   if (p->empty) return EIR_SUCCESS;
   if (l == nullptr || r == nullptr || out == nullptr)
@@ -1049,6 +1099,10 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
   eir::TcParams tp = p->tcp;
   tp.err = ds->err;
   if (peers != nullptr) tp.peers = *peers;
+  if (slab_ctr != nullptr && p->slab_counted) {
+    tp.slab_ctr = slab_ctr;
+    tp.slab_loop = p->slab_loop;
+  }
   ProfScope prof(p, st);
   if (tp.split_k > 1) {
     float *ws = reinterpret_cast<float *>(static_cast<char *>(p->ws) + p->split_ws_offset);
@@ -1058,6 +1112,41 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;
+}
+
+// cuStreamWaitValue32 through the runtime's driver entry-point query (null
+// when the driver does not offer it)
+typedef CUresult (*PfnStreamWaitValue32)(CUstream, CUdeviceptr, cuuint32_t, unsigned int);
+PfnStreamWaitValue32 stream_wait_value32() {
+  static PfnStreamWaitValue32 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void *f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuStreamWaitValue32", &f, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PfnStreamWaitValue32>(f);
+  });
+  return fn;
+}
+
+// frees a plan's gather resources (on the device they were made on)
+void release_gather(eir_plan *p) {
+  int cur = -1;
+  const bool other = p->gather_device >= 0 && cudaGetDevice(&cur) == cudaSuccess && cur != p->gather_device;
+  if (other) cudaSetDevice(p->gather_device);
+  if (p->slab_ctr) cudaFree(p->slab_ctr);
+  if (p->gather_start) cudaEventDestroy(p->gather_start);
+  for (int i = 0; i < eir::kMaxPeers; ++i) {
+    if (p->gather_streams[i]) cudaStreamDestroy(p->gather_streams[i]);
+    if (p->gather_done[i]) cudaEventDestroy(p->gather_done[i]);
+    p->gather_streams[i] = nullptr;
+    p->gather_done[i] = nullptr;
+  }
+  if (other) cudaSetDevice(cur);
+  p->slab_ctr = nullptr;
+  p->gather_start = nullptr;
+  p->gather_device = -1;
 }
 
 // base address of the device allocation holding `ptr` (driver API through
@@ -1103,6 +1192,102 @@ int eir_contract_peers(eir_plan *p, void const *l, void const *r, void const *au
     peers.ptr[i] = peer_outs[i];
   }
   return contract_impl(p, l, r, aux, out, num_peers > 0 ? &peers : nullptr, stream);
+}
+
+int eir_contract_gather(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+                        int32_t num_peers, void *const *peer_outs, void *stream) {
+  if (num_peers < 0 || num_peers > eir::kMaxPeers)
+    return set_error(EIR_INVALID_ARGUMENT, "num_peers must be 0.." + std::to_string(eir::kMaxPeers));
+  if (num_peers > 0 && peer_outs == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null peer list");
+  if (p == nullptr || p->what != 1) return set_error(EIR_INVALID_ARGUMENT, "not a contraction plan");
+  if (num_peers == 0 || p->empty) return contract_impl(p, l, r, aux, out, nullptr, stream);
+  if (p->cpx_inner != nullptr || !p->out_dense)
+    return set_error(EIR_INVALID_ARGUMENT, "eir_contract_gather needs a real plan with a contiguous output");
+  for (int i = 0; i < num_peers; ++i)
+    if (peer_outs[i] == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null peer output");
+  if (out == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null operand pointer");
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const int64_t esize = p->dt_o == EIR_FP64 ? 8 : 4;
+  const int32_t nslab = (int32_t)p->slab_count;
+
+  // per-plan resources on the current device: slab counters, one copy
+  // stream per peer, events joining the copy streams to `stream`
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  if (p->gather_device != dev) {
+    release_gather(p);
+    e = cudaMalloc(&p->slab_ctr, sizeof(uint32_t) * (size_t)std::max<int64_t>(nslab, 1));
+    if (e != cudaSuccess) {
+      p->slab_ctr = nullptr;
+      return cuda_fail(e, "cudaMalloc(slab counters)");
+    }
+    p->gather_device = dev;
+    e = cudaEventCreateWithFlags(&p->gather_start, cudaEventDisableTiming);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+  }
+  for (int i = 0; i < num_peers; ++i) {
+    if (p->gather_streams[i] == nullptr) {
+      e = cudaStreamCreateWithFlags(&p->gather_streams[i], cudaStreamNonBlocking);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamCreate(copy stream)");
+      e = cudaEventCreateWithFlags(&p->gather_done[i], cudaEventDisableTiming);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaEventCreate");
+    }
+  }
+
+  // 1. counters to zero; the copy streams start after that point of `stream`
+  e = cudaMemsetAsync(p->slab_ctr, 0, sizeof(uint32_t) * (size_t)nslab, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaMemsetAsync(slab counters)");
+  e = cudaEventRecord(p->gather_start, st);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  for (int i = 0; i < num_peers; ++i) {
+    e = cudaStreamWaitEvent(p->gather_streams[i], p->gather_start, 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+  }
+  // 2. the contraction; a counting kernel moves slab s's counter to
+  //    slab_target once all of its tiles are stored
+  int rc = contract_impl(p, l, r, aux, out, nullptr, stream, p->slab_ctr);
+  if (rc != EIR_SUCCESS) return rc;
+  // 3. every counter to its final value once the kernel has completed, so
+  //    that no copy below can wait longer than the kernel runs
+  e = eir::launch_slab_release(p->slab_ctr, nslab, p->slab_target, st);
+  if (e != cudaSuccess) return cuda_fail(e, "slab release launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  // 4. per peer, slab by slab: wait for the slab's count, then copy it
+  PfnStreamWaitValue32 wait32 = stream_wait_value32();
+  cudaEvent_t kernel_done = nullptr;
+  if (wait32 == nullptr) {  // no stream memory operations: copy after the kernel
+    kernel_done = p->gather_start;
+    e = cudaEventRecord(kernel_done, st);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+  }
+  const size_t slab_bytes = (size_t)(p->slab_elems * esize);
+  for (int i = 0; i < num_peers; ++i) {
+    cudaStream_t cs = p->gather_streams[i];
+    if (kernel_done != nullptr) {
+      e = cudaStreamWaitEvent(cs, kernel_done, 0);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+    }
+    for (int32_t sl = 0; sl < nslab; ++sl) {
+      const size_t off = (size_t)sl * slab_bytes;
+      if (kernel_done == nullptr) {
+        CUresult cr = wait32(reinterpret_cast<CUstream>(cs),
+                             reinterpret_cast<CUdeviceptr>(p->slab_ctr + sl), p->slab_target,
+                             CU_STREAM_WAIT_VALUE_GEQ);
+        if (cr != CUDA_SUCCESS)
+          return set_error(EIR_CUDA_ERROR, "cuStreamWaitValue32 failed (" + std::to_string((int)cr) + ")");
+      }
+      e = cudaMemcpyAsync(static_cast<char *>(peer_outs[i]) + off, static_cast<char const *>(out) + off,
+                          slab_bytes, cudaMemcpyDeviceToDevice, cs);
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpyAsync(peer slab)");
+    }
+    // 5. `stream` continues once this peer's copies are done
+    e = cudaEventRecord(p->gather_done[i], cs);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaEventRecord");
+    e = cudaStreamWaitEvent(st, p->gather_done[i], 0);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaStreamWaitEvent");
+  }
+  return EIR_SUCCESS;
 }
 
 int eir_copy_to_peers(void const *src, int32_t num_peers, void *const *dsts, int64_t bytes, void *stream) {
@@ -1241,6 +1426,7 @@ int eir_plan_destroy(eir_plan *p) {
   }
   if (p->pre) eir_plan_destroy(p->pre);
   if (p->cpx_inner) eir_plan_destroy(p->cpx_inner);
+  release_gather(p);
   if (p->ws) {
     int cur = 0;
     cudaGetDevice(&cur);

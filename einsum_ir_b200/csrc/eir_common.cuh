@@ -11,6 +11,16 @@
 
 namespace eir {
 
+// TF32 compute: an FP32 value rounded to the nearest TF32 value, ties to even
+// (10 explicit mantissa bits; the 13 low bits cleared). Infinities and NaNs
+// stay as they are. The C oracle models TF32 with the same integer rounding,
+// so the kernels and the oracle multiply identical operands.
+__device__ __forceinline__ uint32_t round_tf32_bits(uint32_t u) {
+  if ((u & 0x7f800000u) == 0x7f800000u) return u;
+  u += 0x0fffu + ((u >> 13) & 1u);
+  return u & 0xffffe000u;
+}
+
 // device-side error word codes (written with atomicCAS, first error wins)
 enum : uint32_t {
   kErrNone = 0,

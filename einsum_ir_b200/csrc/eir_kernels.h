@@ -43,6 +43,10 @@ cudaError_t launch_dmma_contract(bool a_mn, bool b_mn, CUtensorMap const &ma, CU
                                  TcParams const &p, double const *aux, double *out, int num_sms,
                                  cudaStream_t st);
 
+// gathered contraction: sets ctr[0 .. n) to at least `value` after the
+// previous kernel of the stream has completed
+cudaError_t launch_slab_release(uint32_t *ctr, int32_t n, uint32_t value, cudaStream_t st);
+
 // K elements per block (one 128-byte swizzle row): 64 BF16, 32 FP32/TF32, 16 FP64
 int tc_block_k(int kind);
 

@@ -39,6 +39,8 @@ struct SimtParams {
   int32_t last_touch;
   int32_t a_kfast;      // left: K is the fast (stride-1) direction -> load along K
   int32_t b_kfast;      // right: K is the fast direction
+  int32_t round_tf32;   // TF32 compute: FP32 operands rounded to TF32 as they are loaded
+  int32_t pad_;
   int64_t m_tiles, n_tiles;
   PeerOutputs peers;
 };
@@ -97,6 +99,14 @@ struct TcParams {
   int16_t pad_;
   uint32_t *err;                            // device error word
   PeerOutputs peers;
+  // slab completion counters (eir_contract_gather; null otherwise): after
+  // the final stores of a tile, every storing warp adds 1 to
+  // slab_ctr[l[slab_loop]] (slab_ctr[0] when slab_loop < 0), so a copy
+  // engine waiting for a slab's count can move that part of the output while
+  // the kernel computes the next tiles
+  uint32_t *slab_ctr;
+  int32_t slab_loop;
+  int32_t pad2_;
 };
 
 }  // namespace eir

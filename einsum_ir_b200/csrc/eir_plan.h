@@ -90,6 +90,23 @@ struct eir_plan {
   int64_t split_ws_offset = 0;  // split-K partial tiles: ws + this offset
   int ws_device = -1;
 
+  // ---- output gather (eir_contract_gather)
+  bool out_dense = false;         // the output is one contiguous block of out_elems
+  int64_t out_elems = 0;
+  // the output in slabs of its outermost dim when that dim is the kernel's
+  // slowest tile loop (tiles then finish slab by slab), else one slab
+  int64_t slab_count = 1;
+  int64_t slab_elems = 0;
+  int slab_loop = -1;             // tile loop of the slabs
+  bool slab_counted = false;      // the kernel counts each slab's finished tiles
+  uint32_t slab_target = 1;       // count of a finished slab
+  // per-plan gather resources, created on first use on gather_device
+  int gather_device = -1;
+  uint32_t *slab_ctr = nullptr;
+  cudaStream_t gather_streams[eir::kMaxPeers] = {};
+  cudaEvent_t gather_start = nullptr;
+  cudaEvent_t gather_done[eir::kMaxPeers] = {};
+
   // ---- permute (unary COPY) or unary ZERO
   eir::PermuteParams perm;
   bool unary_zero = false;

@@ -251,6 +251,13 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
           }
         }
       }
+      if (p.slab_ctr != nullptr) {
+        // this warp's stores of tile t are visible device-wide before its
+        // slab's count moves: a copy engine waiting on the count reads them
+        __threadfence();
+        __syncwarp();
+        if (lane == 0) atomicAdd(p.slab_ctr + slab_index(c, p.slab_loop), 1u);
+      }
     }
     if (!ok && lane == 0) {
       if (!*abort_flag) record_error(p.err, kErrTimeoutMma);

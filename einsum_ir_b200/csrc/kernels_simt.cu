@@ -34,6 +34,17 @@ __device__ __forceinline__ double to_acc<double, double>(double x) {
   return x;
 }
 
+// an operand value as the accumulation type, rounded to TF32 when the plan
+// computes in TF32 (FP32 operands only)
+template <typename TA, typename T>
+__device__ __forceinline__ TA load_acc(T x, int32_t round_tf32) {
+  return to_acc<TA>(x);
+}
+template <>
+__device__ __forceinline__ float load_acc<float, float>(float x, int32_t round_tf32) {
+  return round_tf32 ? __uint_as_float(round_tf32_bits(__float_as_uint(x))) : x;
+}
+
 __device__ __forceinline__ void decompose(GroupDims const &g, int64_t x, int64_t &ol, int64_t &orr,
                                           int64_t &oo, int64_t &oa) {
   ol = orr = oo = oa = 0;
@@ -125,7 +136,7 @@ __global__ void __launch_bounds__(256)
         kk = e / BM;
       }
       int64_t m = mt * BM + mm, k = k0 + kk;
-      As[kk][mm] = (m < M && k < K) ? to_acc<TA>(L[row_l[mm] + k_l[kk]]) : TA(0);
+      As[kk][mm] = (m < M && k < K) ? load_acc<TA>(L[row_l[mm] + k_l[kk]], p.round_tf32) : TA(0);
     }
 #pragma unroll
     for (int q = 0; q < (BN * BK) / 256; ++q) {
@@ -139,7 +150,7 @@ __global__ void __launch_bounds__(256)
         kk = e / BN;
       }
       int64_t n = nt * BN + nn, k = k0 + kk;
-      Bs[kk][nn] = (n < N && k < K) ? to_acc<TA>(R[col_r[nn] + k_r[kk]]) : TA(0);
+      Bs[kk][nn] = (n < N && k < K) ? load_acc<TA>(R[col_r[nn] + k_r[kk]], p.round_tf32) : TA(0);
     }
     __syncthreads();
 #pragma unroll
@@ -413,6 +424,21 @@ cudaError_t launch_permute(int esize, PermuteParams const &p, void const *in, vo
     case 8: return launch_permute_t<uint64_t>(p, in, out, num_sms, zero, st);
     default: return cudaErrorInvalidValue;
   }
+}
+
+// Sets every slab counter of a gathered contraction to its final value once
+// the contraction kernel before it in the stream has completed (launched
+// without programmatic serialisation, so it starts only after that kernel and
+// its memory writes are complete): every copy that waits for a slab's count
+// is then released, even if the kernel counted fewer tiles (a kernel family
+// that does not count, or one that stopped after a bounded wait gave up).
+__global__ void slab_release_kernel(uint32_t *ctr, int32_t n, uint32_t value) {
+  for (int32_t i = threadIdx.x; i < n; i += blockDim.x) atomicMax(ctr + i, value);
+}
+
+cudaError_t launch_slab_release(uint32_t *ctr, int32_t n, uint32_t value, cudaStream_t st) {
+  slab_release_kernel<<<1, 128, 0, st>>>(ctr, n, value);
+  return cudaGetLastError();
 }
 
 }  // namespace eir

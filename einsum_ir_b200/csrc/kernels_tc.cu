@@ -18,10 +18,11 @@
 // Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+TMEM owner),
 // warps 2..5 = epilogue (TMEM -> registers -> global, fused first/last touch:
 // ZERO/COPY/ADD before, RELU/ADD after, aux read through broadcast strides),
-// warps 6..9 (3xTF32 only) = store lo = x - trunc_TF32(x) of each staged FP32
-// tile next to it in shared memory (the staged x is the hi part, see
-// split_tf32_lo) so three MMAs (lo*hi + hi*lo + hi*hi) give an FP32-accurate
-// product.
+// warps 6..9 (TF32 and 3xTF32) = converters: TF32 rounds each staged FP32
+// tile in place to the nearest TF32 value (round_tf32_inplace); 3xTF32 stores
+// lo = x - trunc_TF32(x) of each staged tile next to it in shared memory (the
+// staged x is the hi part, see split_tf32_lo) so three MMAs (lo*hi + hi*lo +
+// hi*hi) give an FP32-accurate product.
 //
 // Semantics follow the reference loop engine: first touch at the first K
 // step, last touch after the last (ContractionBackend.cpp:296-348,495-515;
@@ -47,9 +48,11 @@ struct TcConfig {
   static constexpr int kABytes = KSUB * kASub;             // per stage
   static constexpr int kBBytes = KSUB * kBSub;
   static constexpr bool kSplit = (KIND == kKind3xTF32);
+  static constexpr bool kRound = (KIND == kKindTF32);      // round staged tiles to TF32 in place
+  static constexpr bool kConv = kSplit || kRound;          // converter warps 6..9
   static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
   static constexpr int kStages = 196608 / kStageBytes;
-  static constexpr int kThreads = kSplit ? 320 : 192;
+  static constexpr int kThreads = kConv ? 320 : 192;
   static constexpr int kTmemCols = 2 * BN;                 // double-buffered accumulator
   static constexpr int kBarBytes = 256;
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + kBarBytes;
@@ -78,7 +81,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
   uint64_t *full = bars;                // S
   uint64_t *empty = bars + S;           // S
-  uint64_t *conv = bars + 2 * S;        // S (split only)
+  uint64_t *conv = bars + 2 * S;        // S (converter warps only)
   uint64_t *tfull = bars + 3 * S;       // 2
   uint64_t *tempty = bars + 3 * S + 2;  // 2
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 4);
@@ -203,7 +206,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           if (ksg >= kr.len) ksg -= kr.len;
           ksg += kr.begin;
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
-          uint64_t *ready = Cfg::kSplit ? &conv[stage] : &full[stage];
+          uint64_t *ready = Cfg::kConv ? &conv[stage] : &full[stage];
           if (!mbar_wait_bounded(ready, phase, abort_flag)) {
             ok = false;
             break;
@@ -310,8 +313,8 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
       if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else if (Cfg::kSplit) {
-    // ------------------------------------------------------------ hi/lo split
+  } else if (Cfg::kConv) {
+    // ------------------------------------------------------------ converters
     const int ct = threadIdx.x - 192;  // 0..127
     int stage = 0;
     uint32_t phase = 0;
@@ -324,13 +327,20 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           break;
         }
         float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
-        float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
-#pragma unroll 4
-        for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32_lo(&a[i], &alo[i]);
         float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
-        float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+        if (Cfg::kSplit) {
+          float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32_lo(&b[i], &blo[i]);
+          for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32_lo(&a[i], &alo[i]);
+          float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32_lo(&b[i], &blo[i]);
+        } else {
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kABytes / 16; i += 128) round_tf32_inplace(&a[i]);
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kBBytes / 16; i += 128) round_tf32_inplace(&b[i]);
+        }
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
         if (++stage == S) {

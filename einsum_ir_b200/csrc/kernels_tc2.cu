@@ -18,11 +18,13 @@
 // Warp roles per CTA: warp 0 = TMA producer, warp 1 = MMA issuer (leader) and
 // TMEM owner (both CTAs allocate with cta_group::2), warps 2..9 = epilogue, two
 // per TMEM lane quadrant with half of the columns each (fused first / last
-// touch as in the one-CTA kernel). FP32-exact mode (3xTF32): warps 2..5 =
-// epilogue, warps 6..9 split each CTA's staged FP32 tiles into hi / lo TF32
-// parts; the loads of a CTA then complete on its own barrier and the MMA
-// issuer waits for the converter warps of both CTAs. Every wait is bounded;
-// a timeout raises the abort flag in both CTAs and records a device error.
+// touch as in the one-CTA kernel). TF32 and FP32-exact (3xTF32) modes: warps
+// 2..5 = epilogue, warps 6..9 = converters, which round each CTA's staged FP32
+// tiles in place to the nearest TF32 value (TF32) or split them into hi / lo
+// TF32 parts (3xTF32); the loads of a CTA then complete on its own barrier
+// and the MMA issuer waits for the converter warps of both CTAs. Every wait
+// is bounded; a timeout raises the abort flag in both CTAs and records a
+// device error.
 #include <cuda.h>
 #include "eir_common.cuh"
 #include "eir_params.h"
@@ -46,14 +48,16 @@ struct PairConfig {
   static constexpr int kBBytes = KSUB * kBSub;
   // FP32-exact mode keeps a hi and a lo TF32 copy of every staged operand
   static constexpr bool kSplit = (KIND == kKind3xTF32);
+  static constexpr bool kRound = (KIND == kKindTF32);  // round staged tiles to TF32 in place
+  static constexpr bool kConv = kSplit || kRound;      // converter warps
   static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
   static constexpr int kMaxStages = 8;
   static constexpr int kFit = (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
-  // epilogue: 2 warps per TMEM lane quadrant (half the columns each), or 1 in
-  // FP32-exact mode, whose 4 converter warps split the staged tiles
-  static constexpr int kEpiWarps = kSplit ? 4 : 8;
-  static constexpr int kConvWarps = kSplit ? 4 : 0;
+  // epilogue: 2 warps per TMEM lane quadrant (half the columns each), or 1
+  // next to the 4 converter warps of the TF32 / FP32-exact modes
+  static constexpr int kEpiWarps = kConv ? 4 : 8;
+  static constexpr int kConvWarps = kConv ? 4 : 0;
   static constexpr int kThreads = 32 * (2 + kEpiWarps + kConvWarps);
   static constexpr int kTmemCols = 2 * BN;         // double-buffered accumulator
   static constexpr int kSmemBytes = 1024 + kStages * kStageBytes + 512;
@@ -81,12 +85,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
   uint8_t *sAlo = sB + S * Cfg::kBBytes;                       // (split) S x kABytes
   uint8_t *sBlo = sAlo + (Cfg::kSplit ? S * Cfg::kABytes : 0);  // (split) S x kBBytes
   uint64_t *bars = reinterpret_cast<uint64_t *>(smem + S * Cfg::kStageBytes);
-  uint64_t *full = bars;                // S (leader's count both CTAs' bytes; split: own bytes)
+  uint64_t *full = bars;                // S (leader's count both CTAs' bytes; converters: own bytes)
   uint64_t *empty = bars + S;           // S
   uint64_t *tfull = bars + 2 * S;       // 2
   uint64_t *tempty = bars + 2 * S + 2;  // 2 (leader's: epilogue warps of both CTAs)
   uint64_t *drain = bars + 2 * S + 4;   // 1 (leader: all MMAs done)
-  uint64_t *conv = bars + 2 * S + 5;    // S (split, leader's: converter warps of both CTAs)
+  uint64_t *conv = bars + 2 * S + 5;    // S (converters, leader's: converter warps of both CTAs)
   uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(bars + 3 * S + 5);
   volatile int *abort_flag = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
@@ -176,11 +180,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
             break;
           }
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
-          // FP32-exact mode: each CTA's loads complete on its own barrier (its
-          // converter warps wait there); otherwise on the leader's, for both
-          if (Cfg::kSplit) mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
+          // with converter warps each CTA's loads complete on its own barrier
+          // (its converters wait there); otherwise on the leader's, for both
+          if (Cfg::kConv) mbar_arrive_expect_tx(&full[stage], nsub * (Cfg::kASub + Cfg::kBSub));
           else if (rank == 0) mbar_arrive_expect_tx(&full[stage], 2 * nsub * (Cfg::kASub + Cfg::kBSub));
-          const uint32_t bar = Cfg::kSplit ? smem_u32(&full[stage]) : full_leader + 8u * (uint32_t)stage;
+          const uint32_t bar = Cfg::kConv ? smem_u32(&full[stage]) : full_leader + 8u * (uint32_t)stage;
           for (int sub = 0; sub < nsub; ++sub, kw.next(p))
             k_block(kw, sA + stage * Cfg::kABytes + sub * Cfg::kASub,
                     sB + stage * Cfg::kBBytes + sub * Cfg::kBSub, bar);
@@ -236,7 +240,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
           int ksg = js + rot;
           if (ksg >= n_kstages) ksg -= n_kstages;
           const int nsub = min(KSUB, p.k_steps - ksg * KSUB);
-          if (!mbar_wait_bounded(Cfg::kSplit ? &conv[stage] : &full[stage], phase, abort_flag)) {
+          if (!mbar_wait_bounded(Cfg::kConv ? &conv[stage] : &full[stage], phase, abort_flag)) {
             ok = false;
             break;
           }
@@ -343,10 +347,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else if (Cfg::kSplit) {
-    // ------------------------------------------------------------ hi/lo split (both CTAs)
-    // each CTA splits its own staged halves, then every converter warp of the
-    // pair arrives on the leader's conv barrier, which the MMA issuer waits on
+  } else if (Cfg::kConv) {
+    // ------------------------------------------------------------ converters (both CTAs)
+    // each CTA rounds or splits its own staged halves, then every converter
+    // warp of the pair arrives on the leader's conv barrier, which the MMA
+    // issuer waits on
     const int ct = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);  // 0 .. 32 * kConvWarps - 1
     constexpr int kCt = 32 * Cfg::kConvWarps;
     const uint32_t conv_leader = mapa_shared(smem_u32(conv), 0);
@@ -360,13 +365,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
           break;
         }
         float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
-        float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
-#pragma unroll 4
-        for (int i = ct; i < Cfg::kABytes / 16; i += kCt) split_tf32_lo(&a[i], &alo[i]);
         float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
-        float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+        if (Cfg::kSplit) {
+          float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
 #pragma unroll 4
-        for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) split_tf32_lo(&b[i], &blo[i]);
+          for (int i = ct; i < Cfg::kABytes / 16; i += kCt) split_tf32_lo(&a[i], &alo[i]);
+          float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) split_tf32_lo(&b[i], &blo[i]);
+        } else {
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kABytes / 16; i += kCt) round_tf32_inplace(&a[i]);
+#pragma unroll 4
+          for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) round_tf32_inplace(&b[i]);
+        }
         fence_proxy_async_smem();  // the tensor cores read these tiles
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(conv_leader + 8u * (uint32_t)stage);

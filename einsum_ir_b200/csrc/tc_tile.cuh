@@ -3,6 +3,7 @@
 #pragma once
 
 #include <cstdint>
+#include "eir_common.cuh"
 #include "eir_params.h"
 
 namespace eir {
@@ -49,6 +50,17 @@ __device__ __forceinline__ TileCoord decode_tile(TcParams const &p, int64_t tile
     }
   }
   return c;
+}
+
+// Tile-loop index of a tile coordinate for a run-time loop number (no
+// dynamically indexed register array).
+template <typename Coord>
+__device__ __forceinline__ int slab_index(Coord const &c, int slab_loop) {
+  int s = 0;
+#pragma unroll
+  for (int i = 0; i < kMaxTileLoops; ++i)
+    if (i == slab_loop) s = c.l[i];
+  return s;
 }
 
 __device__ __forceinline__ int src_coord(int8_t src, int ko0, int ko1, TileCoord const &c) {
@@ -175,6 +187,18 @@ __device__ __forceinline__ void split_tf32_lo(float4 const *x_in, float4 *lo_out
   const float4 x = *x_in;
   auto lo = [](float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); };
   *lo_out = make_float4(lo(x.x), lo(x.y), lo(x.z), lo(x.w));
+}
+
+// TF32 mode: each staged FP32 operand is rounded in place to the nearest TF32
+// value (round_tf32_bits) before the tensor core reads it, which would
+// otherwise ignore the 13 low mantissa bits (truncation).
+__device__ __forceinline__ void round_tf32_inplace(float4 *x_io) {
+  uint4 u = *reinterpret_cast<uint4 *>(x_io);
+  u.x = round_tf32_bits(u.x);
+  u.y = round_tf32_bits(u.y);
+  u.z = round_tf32_bits(u.z);
+  u.w = round_tf32_bits(u.w);
+  *reinterpret_cast<uint4 *>(x_io) = u;
 }
 
 // Epilogue variant of a plan: 0 = ZERO first touch and no last touch, 1 = COPY

@@ -153,6 +153,28 @@ int     eir_contract_peers(eir_plan *plan, void const *left, void const *right,
                            void const *out_aux, void *out, int32_t num_peers,
                            void *const *peer_outs, void *stream);
 
+/* Same contraction as eir_contract, followed by the all-gather step of a
+ * sharded contraction: the finished output is copied, at the same byte
+ * offsets, into each of num_peers (<= 7) other buffers of out's extent
+ * (typically this rank's block inside the full outputs of the other GPUs,
+ * mapped with eir_ipc_open_handle). The copies run on the copy engines, one
+ * stream per peer owned by the plan, so they take no SM from the
+ * contraction. When the output's outermost dim is the kernel's slowest tile
+ * loop and the kernel publishes per-slab completion (FP64 plans on the DMMA
+ * kernel), the copy of each slab of that dim starts as soon as the kernel has
+ * stored it, overlapping the slabs still being computed; otherwise the
+ * copies start when the kernel ends. The output must be one contiguous
+ * block. Asynchronous on `stream`: once `stream` has passed the call, the
+ * output and every peer copy are complete; a reader on another GPU first
+ * synchronises with this rank (e.g. a stream synchronisation, then a
+ * cross-process barrier). Like every workspace-owning plan, one plan must
+ * not run on two streams at once. Not for complex plans. No counterpart in
+ * the reference (it has no multi-GPU path; BASELINE config 5 shards its
+ * batch dim z across GPUs and all-gathers the output). */
+int     eir_contract_gather(eir_plan *plan, void const *left, void const *right,
+                            void const *out_aux, void *out, int32_t num_peers,
+                            void *const *peer_outs, void *stream);
+
 /* CUDA IPC of device buffers between the processes of one node (one process
  * per GPU): a handle (EIR_IPC_HANDLE_BYTES opaque bytes) and offset for a
  * pointer into any cudaMalloc'd allocation; the opening process gets the

@@ -5,8 +5,9 @@ matmul, bias broadcasts, batched C dims, ZERO+RELU, permuted operands) and the
 BASELINE configs at reduced sizes. Tolerances are relative Frobenius errors
 against the oracle evaluated on the same inputs: BF16 inputs with FP32
 accumulation 1e-5 (north_star allows 1e-2), FP32-accurate (3xTF32 / SIMT FP32)
-1e-5 (north_star: 1e-4), TF32 on TF32-representable inputs 1e-5, TF32 on
-general FP32 inputs 2e-3, FP64 1e-12.
+1e-5 (north_star: 1e-4), TF32 1e-5 (the kernels round every FP32 operand to
+the nearest TF32 value, ties to even, as the oracle's TF32 model does, on
+TF32-representable and on general FP32 inputs), FP64 1e-12.
 """
 from __future__ import annotations
 
@@ -20,7 +21,7 @@ from tests import _oracle
 
 pytestmark = pytest.mark.gpu
 
-TOL = {"bf16": 1e-5, "fp32": 1e-5, "tf32": 1e-5, "tf32_general": 2e-3, "fp64": 1e-12}
+TOL = {"bf16": 1e-5, "fp32": 1e-5, "tf32": 1e-5, "tf32_general": 1e-5, "fp64": 1e-12}
 
 
 def _make_inputs(torch, shape_l, shape_r, dtype, seed, tf32_exact):
@@ -215,9 +216,19 @@ def test_tc_split_k(cuda, expr, sizes, dtype, first, last, aux):
     assert "splitk=" in d and "splitk=1 " not in d and "pair" not in d, d
 
 
-def test_tc_tf32_general_inputs(cuda):
-    run_case(cuda, "km,nk->nm", dict(m=256, n=256, k=256), "tf32", tf32_general=True,
-             expect_family=TC)
+@pytest.mark.parametrize("expr,pair", [("km,nk->nm", 0), ("km,nk->nm", 1), ("mk,kn->nm", 1),
+                                       ("zcdef,zabcd->zabef", None)])
+def test_tc_tf32_general_inputs(cuda, expr, pair):
+    # general FP32 inputs: the kernels round every operand to the nearest TF32
+    # value (ties to even) in shared memory, the oracle's TF32 model
+    sizes = dict(m=256, n=256, k=256) if "m" in expr else dict(z=3, a=8, b=8, c=8, d=8, e=8, f=8)
+    run_case(cuda, expr, sizes, "tf32", tf32_general=True, expect_family=TC, pair=pair)
+
+
+def test_simt_tf32_general_inputs(cuda):
+    # the CUDA-core kernel rounds its TF32 operands as they are loaded
+    run_case(cuda, "zab,zbc->zac", dict(z=5, a=7, b=9, c=6), "tf32", tf32_general=True,
+             expect_family=SIMT, tc_min_ops=str(1 << 40))
 
 
 @pytest.mark.parametrize("dtype", ["fp32", "bf16", "tf32"])

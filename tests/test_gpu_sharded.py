@@ -1,7 +1,8 @@
 """Batch-sharded config 5 on two GPUs through torchrun (einsum_ir_b200.sharded):
-the fused gather (every rank's epilogue stores into all ranks' outputs over
-NVLink) and the NCCL all-gather path, each spot-checked by rank 0 against a
-torch contraction of another rank's block. Skipped with fewer than 2 GPUs."""
+the copy-engine gather of finished z-slabs (eir_contract_gather, FP64 and
+TF32), the fused gather (every rank's epilogue stores into all ranks' outputs
+over NVLink) and the NCCL all-gather path, each checked on one z-slab of every
+rank's block against torch. Skipped with fewer than 2 GPUs."""
 from __future__ import annotations
 
 import json
@@ -32,3 +33,5 @@ def test_sharded_two_ranks(args, tol):
     res = json.loads(line)
     assert res["gpus"] == 2 and res["rel_err_check"] <= tol, res
     assert ("NCCL" in res["gather"]) == ("--nccl" in args), res
+    if not args or args == ["--fp32", "--tf32"]:
+        assert "copy engines" in res["gather"], res

@@ -1,10 +1,10 @@
 """Multi-process logic on CPU (gloo, world size 2): the block layout of the
 batch-sharded contraction and the bench's max-over-ranks timing reduction.
-The per-block compute is torch.einsum on CPU here; on GPUs it is the C-ABI
-plan (einsum_ir_b200.sharded.ShardedContraction)."""
+The per-block compute is torch.einsum on CPU here, and the gather a gloo
+all-gather; on GPUs the compute is the C-ABI plan and the gather the copy
+engines (einsum_ir_b200.sharded.ShardedContraction.run_gather)."""
 from __future__ import annotations
 
-import os
 import socket
 
 import pytest
@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from einsum_ir_b200.sharded import ShardLayout, run_sharded
+from einsum_ir_b200.sharded import ShardLayout
 
 
 def _free_port():
@@ -21,26 +21,23 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _worker(rank, world, port, chunks, q):
+def _worker(rank, world, port, q):
     dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
                             world_size=world)
     g = torch.Generator().manual_seed(0)
-    z = 4 * world * chunks
+    z = 6 * world
     left = torch.rand(z, 3, 2, 4, generator=g, dtype=torch.float64)   # zabc
     right = torch.rand(z, 4, 5, generator=g, dtype=torch.float64)     # zcd
     out = torch.full((z, 3, 2, 5), float("nan"), dtype=torch.float64)
-    lay = ShardLayout(z, world, chunks)
-
-    def compute(c, start):
-        sl = slice(start, start + lay.block)
-        return torch.einsum("zabc,zcd->zabd", left[sl], right[sl]).contiguous()
-
-    def gather(dst, local):
-        parts = [torch.empty_like(local) for _ in range(world)]
-        dist.all_gather(parts, local)
-        dst.copy_(torch.cat(parts, 0))
-
-    run_sharded(lay, rank, compute, lambda rg: out[rg.start:rg.stop], gather)
+    lay = ShardLayout(z, world)
+    rg = lay.owned(rank)
+    # this rank's block into its place, then every block into every rank's output
+    out[rg.start:rg.stop] = torch.einsum("zabc,zcd->zabd", left[rg.start:rg.stop], right[rg.start:rg.stop])
+    parts = [torch.empty_like(out[rg.start:rg.stop]) for _ in range(world)]
+    dist.all_gather(parts, out[rg.start:rg.stop].contiguous())
+    for r, p in enumerate(parts):
+        o = lay.owned(r)
+        out[o.start:o.stop] = p
     ref = torch.einsum("zabc,zcd->zabd", left, right)
     err = float((out - ref).abs().max())
     # bench-style timing reduction: the max over ranks
@@ -51,13 +48,12 @@ def _worker(rank, world, port, chunks, q):
     dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("chunks", [1, 3])
-def test_sharded_layout_and_gather_gloo(chunks):
+def test_sharded_layout_and_gather_gloo():
     world = 2
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, chunks, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, q)) for r in range(world)]
     for p in procs:
         p.start()
     res = [q.get(timeout=120) for _ in range(world)]
@@ -71,11 +67,8 @@ def test_sharded_layout_and_gather_gloo(chunks):
 
 def test_shard_layout_covers_every_index_once():
     for world in (1, 2, 4, 8):
-        for chunks in (1, 2, 4):
-            lay = ShardLayout(64, world, chunks)
-            owned = sorted(s + i for r in range(world) for s in lay.owned(r) for i in range(lay.block))
-            assert owned == list(range(64))
-            for c in range(chunks):
-                rg = lay.gathered_range(c)
-                starts = sorted(lay.owned(r)[c] for r in range(world))
-                assert starts[0] == rg.start and rg.stop == starts[-1] + lay.block
+        lay = ShardLayout(64, world)
+        owned = [i for r in range(world) for i in lay.owned(r)]
+        assert owned == list(range(64))  # contiguous blocks in rank order (NCCL all-gather order)
+    with pytest.raises(ValueError):
+        ShardLayout(64, 3).block
