@@ -245,6 +245,17 @@ def _fp64_peak(dev):
     return 2.0 * n ** 3 / (best * 1e-3) / 1e12
 
 
+def _profile_traffic():
+    """DRAM bytes of one bench launch of the DMMA kernel, from the committed ncu
+    summary (a z = 8 capture scaled by the z-slabs a launch processes)"""
+    import re
+    f = ROOT / "profiles" / "dmma_contract_fp64_cfg5_z8.txt"
+    if not f.exists():
+        return None
+    m = re.search(r"bench_launch_traffic_bytes:\s*([0-9.eE+]+)", f.read_text())
+    return float(m.group(1)) if m else None
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -415,8 +426,13 @@ def run_ours(args):
                     "pipeline": f"{n_groups} groups of {gz} z-slab(s): H2D / contraction / D2H on "
                                 "three streams", "d2h_check_max_abs_diff": e2e_rel},
             "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                         "frac": achieved / peak, "traffic": None,
-                         "kernel": "eir::dmma_contract_kernel<false,true> (FP64 DMMA)",
+                         "frac": achieved / peak,
+                         "traffic": (_profile_traffic() / world) if _profile_traffic() else None,
+                         "traffic_source": "profiles/dmma_contract_fp64_cfg5_z8.txt (ncu z=8 capture, "
+                                           "scaled by the z-slabs of this launch)",
+                         "kernel": "eir::dmma_contract_kernel<%s,%s> (FP64 DMMA)" % (
+                             "true" if "A=MN" in plan.describe() else "false",
+                             "true" if "B=MN" in plan.describe() else "false"),
                          "peak_source": "cuBLAS DGEMM 8192^3 (torch.matmul FP64) measured in this run, best "
                                         "of 5 (MEASURED_PEAKS.json has no FP64 figure)",
                          "kernel_ms": kern_ms_avg,

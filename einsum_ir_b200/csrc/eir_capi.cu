@@ -254,18 +254,12 @@ int plan_permute(int nd, int64_t const *sizes, int64_t const *sin, int64_t const
     pp->mode = 1;
     pp->tdim_in = tin;
     pp->batch = total / (d[0].size * d[tin].size);
-    if (text) *text = "permute: 32x32 tile transpose, nd=" + std::to_string(pp->nd);
+    if (text) *text = "permute: 64x64 tile transpose, nd=" + std::to_string(pp->nd);
   }
   return EIR_SUCCESS;
 }
 
 // ------------------------------------------------------------- TC lowering
-struct TcChoice {
-  bool ok = false;
-  int prepack = -1;                 // operand to pre-permute (0 left, 1 right)
-  std::vector<int64_t> pre_order;   // prepack: dim indices, outermost first
-};
-
 int dim_index_with_unit_stride(std::vector<LDim> const &d, int type, bool left) {
   for (int i = 0; i < (int)d.size(); ++i)
     if (d[i].type == type && (left ? d[i].sl : d[i].sr) == 1) return i;
@@ -393,31 +387,41 @@ bool try_tc(eir_plan *p, std::string *why) {
         np = i;
   }
 
-  // pre-permute: packed layout of the operand with its dims in descending
-  // stride order, except the primitive K dim which becomes innermost
-  std::vector<int64_t> packed_stride(d.size(), 0);
-  if (prepack >= 0) {
-    bool left = prepack == 0;
+  // Operand copies into the plan's workspace, one per operand at most:
+  //  * K-order mismatch (prepack): the operand re-laid out with its dims in
+  //    descending stride order except the primitive K dim, which becomes
+  //    innermost (the operand is K-major afterwards);
+  //  * TF32 compute: each FP32 operand rounded to the nearest TF32 value
+  //    (ties to even) while it is copied, dims kept in their order, so the
+  //    tensor cores (which ignore the 13 low mantissa bits of an FP32 word)
+  //    multiply exactly the TF32-rounded operands of the oracle's model.
+  const bool round_tf32 = kind == 1;
+  const bool copy_l = prepack == 0 || round_tf32, copy_r = prepack == 1 || round_tf32;
+  auto packed_layout = [&](bool left, bool k_inner) {
+    std::vector<int64_t> ps(d.size(), 0);
     std::vector<int> ids;
     for (int i = 0; i < (int)d.size(); ++i)
       if (d[i].type == EIR_DIM_C || d[i].type == EIR_DIM_K ||
           d[i].type == (left ? EIR_DIM_M : EIR_DIM_N))
-        if (i != kp) ids.push_back(i);
+        if (!(k_inner && i == kp)) ids.push_back(i);
     std::stable_sort(ids.begin(), ids.end(), [&](int a, int b) {
       return std::llabs(left ? d[a].sl : d[a].sr) > std::llabs(left ? d[b].sl : d[b].sr);
     });
-    ids.push_back(kp);
+    if (k_inner) ids.push_back(kp);
     int64_t s = 1;
     for (int j = (int)ids.size() - 1; j >= 0; --j) {
-      packed_stride[ids[j]] = s;
+      ps[ids[j]] = s;
       s *= d[ids[j]].size;
     }
-    // if the packed operand is MN-major (other operand MN-major, kp innermost) it is K-major now
-    if (left) a_mn = false;
-    else b_mn = false;
-  }
-  auto sl_of = [&](int i) { return prepack == 0 ? packed_stride[i] : d[i].sl; };
-  auto sr_of = [&](int i) { return prepack == 1 ? packed_stride[i] : d[i].sr; };
+    return ps;
+  };
+  const std::vector<int64_t> packed_l = copy_l ? packed_layout(true, prepack == 0) : std::vector<int64_t>();
+  const std::vector<int64_t> packed_r = copy_r ? packed_layout(false, prepack == 1) : std::vector<int64_t>();
+  // a re-laid-out operand is K-major now (the kept-order TF32 copy keeps its major-ness)
+  if (prepack == 0) a_mn = false;
+  if (prepack == 1) b_mn = false;
+  auto sl_of = [&](int i) { return copy_l ? packed_l[i] : d[i].sl; };
+  auto sr_of = [&](int i) { return copy_r ? packed_r[i] : d[i].sr; };
 
   // outer K dims and tile loops
   std::vector<int> ko, loops;
@@ -640,43 +644,52 @@ bool try_tc(eir_plan *p, std::string *why) {
   p->tc_esize = esize;
   p->prepack = prepack;
 
-  if (prepack >= 0) {
-    bool left = prepack == 0;
+  // the operand copies' permute plans and their places in the workspace
+  p->ws_bytes = 0;
+  for (int side = 0; side < 2; ++side) {
+    const bool left = side == 0;
+    if (!(left ? copy_l : copy_r)) continue;
+    std::vector<int64_t> const &ps = left ? packed_l : packed_r;
     std::vector<int64_t> sz, si, so;
     for (int i = 0; i < (int)d.size(); ++i)
       if (d[i].type == EIR_DIM_C || d[i].type == EIR_DIM_K ||
           d[i].type == (left ? EIR_DIM_M : EIR_DIM_N)) {
         sz.push_back(d[i].size);
         si.push_back(left ? d[i].sl : d[i].sr);
-        so.push_back(packed_stride[i]);
+        so.push_back(ps[i]);
       }
     eir_plan *pre = nullptr;
     int rc = eir_permute_plan_create((int32_t)sz.size(), sz.data(), si.data(), so.data(),
                                      left ? p->dt_l : p->dt_r, &pre);
     if (rc != EIR_SUCCESS) {
-      *why = "pre-permute planning failed";
+      *why = "operand copy planning failed";
+      if (p->pre_l) eir_plan_destroy(p->pre_l);
+      p->pre_l = nullptr;
       p->tc = false;
       return false;
     }
-    p->pre = pre;
-    p->ws_bytes = bytes_of(left);
+    pre->perm.round_tf32 = round_tf32 ? 1 : 0;
+    (left ? p->pre_l : p->pre_r) = pre;
+    (left ? p->ws_off_l : p->ws_off_r) = p->ws_bytes;
+    p->ws_bytes = (p->ws_bytes + bytes_of(left) + 255) / 256 * 256;
   }
   if (t.split_k > 1) {
-    p->split_ws_offset = (p->ws_bytes + 255) / 256 * 256;
+    p->split_ws_offset = p->ws_bytes;
     p->ws_bytes = p->split_ws_offset + (int64_t)t.split_k * t.ws_slice * 4;
   }
 
   char buf[512];
   std::snprintf(buf, sizeof(buf),
                 "tc kind=%s %sBN=%d KSUB=%d A=%s B=%s M=%lld N=%lld Kp=%lld ko=%lldx%lld loops=%d "
-                "tiles=%lld ksteps=%d prepack=%s splitk=%d",
+                "tiles=%lld ksteps=%d prepack=%s splitk=%d%s",
                 kind == 0 ? "bf16" : kind == 1 ? "tf32" : kind == 2 ? "3xtf32" : "fp64-dmma",
                 pair ? "pair BM=256 " : "", bn,
                 p->tc_ksub, a_mn ? "MN" : "K",
                 b_mn ? "MN" : "K", (long long)t.m_size, (long long)t.n_size, (long long)t.kp_size,
                 (long long)t.ko_size[0], (long long)t.ko_size[1], t.n_loops,
                 (long long)t.total_tiles, t.k_steps,
-                prepack < 0 ? "none" : (prepack == 0 ? "left" : "right"), (int)t.split_k);
+                prepack < 0 ? "none" : (prepack == 0 ? "left" : "right"), (int)t.split_k,
+                round_tf32 ? " tf32-rounded-copies" : "");
   *why = buf;
   return true;
 }
@@ -1011,9 +1024,32 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
 
 namespace {
 
-// eir_contract, with optional peer copies of the output (eir_contract_peers)
+// one launch of a permute plan (no device-state lookup, nothing allocated)
+int run_permute(eir_plan *p, void const *in, void *out, int num_sms, cudaStream_t st) {
+  eir::PermuteParams pp = p->perm;
+  if (pp.mode == 0 && pp.vec > 1 &&
+      ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % (pp.vec * p->esize)))
+    pp.vec = 1;
+  ProfScope prof(p, st);
+  cudaError_t e = eir::launch_permute(p->esize, pp, in, out, num_sms, st, p->unary_zero);
+  if (e != cudaSuccess) return cuda_fail(e, "permute launch");
+  g_launches.fetch_add(1, std::memory_order_relaxed);
+  return EIR_SUCCESS;
+}
+
+bool takes_tensor_cores(eir_plan const *p, void const *l, void const *r) {
+  // TMA needs 16-byte aligned bases; otherwise the generic path reads the operands
+  return (p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA) &&
+         !((reinterpret_cast<uintptr_t>(l) | reinterpret_cast<uintptr_t>(r)) & 15);
+}
+
+// eir_contract and its variants (eir::api_contract): peer outputs
+// (eir_contract_peers), slab counters (eir_contract_gather), and a caller's
+// workspace, error word and SM count (eir_contract_no_alloc, which must not
+// reach an allocation: ws_ext / err_ext non-null)
 int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
-                  eir::PeerOutputs const *peers, void *stream, uint32_t *slab_ctr = nullptr) {
+                  eir::PeerOutputs const *peers, void *stream, uint32_t *slab_ctr = nullptr,
+                  void *ws_ext = nullptr, uint32_t *err_ext = nullptr, int num_sms_ext = 0) {
   if (p == nullptr || p->what != 1) return set_error(EIR_INVALID_ARGUMENT, "not a contraction plan");
   if (p->empty) return EIR_SUCCESS;
   if (l == nullptr || r == nullptr || out == nullptr)
@@ -1022,6 +1058,7 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
   if (uses_aux && aux == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->cpx_inner != nullptr) {
+    if (ws_ext != nullptr) return set_error(EIR_INVALID_ARGUMENT, "complex plans need their own workspace");
     // complex: expand the right operand into the workspace, then the real plan
     int dev = 0;
     cudaGetDevice(&dev);
@@ -1043,18 +1080,19 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
     g_launches.fetch_add(1, std::memory_order_relaxed);
     return contract_impl(p->cpx_inner, l, p->ws, aux, out, peers, stream);
   }
-  if (p->family != EIR_FAMILY_TC && p->family != EIR_FAMILY_DMMA)
-    return run_simt(p, l, r, aux, out, peers, st);
+  if (!takes_tensor_cores(p, l, r)) return run_simt(p, l, r, aux, out, peers, st);
 
-  DeviceState *ds = nullptr;
-  int rc = device_state(&ds);
-  if (rc != EIR_SUCCESS) return rc;
-  // TMA needs 16-byte aligned bases; otherwise take the generic path
-  if ((reinterpret_cast<uintptr_t>(l) & 15) || (reinterpret_cast<uintptr_t>(r) & 15))
-    return run_simt(p, l, r, aux, out, peers, st);
-
-  void const *a_ptr = l, *b_ptr = r;
-  if (p->ws_bytes > 0) {  // pre-permuted operand and / or split-K partial tiles
+  uint32_t *err = err_ext;
+  int num_sms = num_sms_ext;
+  if (err == nullptr) {
+    DeviceState *ds = nullptr;
+    int rc = device_state(&ds);
+    if (rc != EIR_SUCCESS) return rc;
+    err = ds->err;
+    num_sms = ds->num_sms;
+  }
+  char *ws = static_cast<char *>(ws_ext);
+  if (p->ws_bytes > 0 && ws == nullptr) {  // operand copies and / or split-K partial tiles
     int dev = 0;
     cudaGetDevice(&dev);
     if (p->ws == nullptr || p->ws_device != dev) {
@@ -1066,12 +1104,19 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
       }
       p->ws_device = dev;
     }
+    ws = static_cast<char *>(p->ws);
   }
-  if (p->prepack >= 0) {
-    void const *src = p->prepack == 0 ? l : r;
-    rc = eir_permute(p->pre, src, p->ws, stream);
+  void const *a_ptr = l, *b_ptr = r;
+  int rc = EIR_SUCCESS;
+  if (p->pre_l != nullptr) {
+    rc = run_permute(p->pre_l, l, ws + p->ws_off_l, num_sms, st);
     if (rc != EIR_SUCCESS) return rc;
-    (p->prepack == 0 ? a_ptr : b_ptr) = p->ws;
+    a_ptr = ws + p->ws_off_l;
+  }
+  if (p->pre_r != nullptr) {
+    rc = run_permute(p->pre_r, r, ws + p->ws_off_r, num_sms, st);
+    if (rc != EIR_SUCCESS) return rc;
+    b_ptr = ws + p->ws_off_r;
   }
 
   CUtensorMap ma, mb;
@@ -1097,7 +1142,7 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
     mb = p->cache_b.map;
   }
   eir::TcParams tp = p->tcp;
-  tp.err = ds->err;
+  tp.err = err;
   if (peers != nullptr) tp.peers = *peers;
   if (slab_ctr != nullptr && p->slab_counted) {
     tp.slab_ctr = slab_ctr;
@@ -1105,10 +1150,10 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
   }
   ProfScope prof(p, st);
   if (tp.split_k > 1) {
-    float *ws = reinterpret_cast<float *>(static_cast<char *>(p->ws) + p->split_ws_offset);
-    return eir::api_launch_tc_split(p, ma, mb, tp, aux, out, ws, ds->num_sms, st);
+    float *part = reinterpret_cast<float *>(ws + p->split_ws_offset);
+    return eir::api_launch_tc_split(p, ma, mb, tp, aux, out, part, num_sms, st);
   }
-  cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, ds->num_sms, st);
+  cudaError_t e = eir::api_launch_tc(p, ma, mb, tp, aux, out, num_sms, st);
   if (e != cudaSuccess) return cuda_fail(e, "tc contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;
@@ -1171,6 +1216,17 @@ int allocation_base(void const *ptr, char **base) {
 }
 
 }  // namespace
+
+namespace eir {
+int api_contract(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+                 PeerOutputs const *peers, void *stream, uint32_t *slab_ctr, void *ws, uint32_t *err,
+                 int num_sms) {
+  return contract_impl(p, l, r, aux, out, peers, stream, slab_ctr, ws, err, num_sms);
+}
+int64_t api_workspace_needed(eir_plan const *p, void const *l, void const *r) {
+  return takes_tensor_cores(p, l, r) ? p->ws_bytes : 0;
+}
+}  // namespace eir
 
 extern "C" {
 
@@ -1383,16 +1439,7 @@ int eir_permute(eir_plan *p, void const *in, void *out, void *stream) {
   DeviceState *ds = nullptr;
   int rc = device_state(&ds);
   if (rc != EIR_SUCCESS) return rc;
-  eir::PermuteParams pp = p->perm;
-  if (pp.mode == 0 && pp.vec > 1 &&
-      ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) % (pp.vec * p->esize)))
-    pp.vec = 1;
-  ProfScope prof(p, static_cast<cudaStream_t>(stream));
-  cudaError_t e = eir::launch_permute(p->esize, pp, in, out, ds->num_sms,
-                                      static_cast<cudaStream_t>(stream), p->unary_zero);
-  if (e != cudaSuccess) return cuda_fail(e, "permute launch");
-  g_launches.fetch_add(1, std::memory_order_relaxed);
-  return EIR_SUCCESS;
+  return run_permute(p, in, out, ds->num_sms, static_cast<cudaStream_t>(stream));
 }
 
 int eir_plan_profile(eir_plan *p, int32_t enable) {
@@ -1424,7 +1471,8 @@ int eir_plan_destroy(eir_plan *p) {
     cudaEventDestroy(ev.first);
     cudaEventDestroy(ev.second);
   }
-  if (p->pre) eir_plan_destroy(p->pre);
+  if (p->pre_l) eir_plan_destroy(p->pre_l);
+  if (p->pre_r) eir_plan_destroy(p->pre_r);
   if (p->cpx_inner) eir_plan_destroy(p->cpx_inner);
   release_gather(p);
   if (p->ws) {
@@ -1445,19 +1493,33 @@ int64_t eir_plan_workspace_bytes(eir_plan const *p) { return p ? p->ws_bytes : 0
 char const *eir_plan_describe(eir_plan const *p) { return p ? p->text.c_str() : ""; }
 
 int eir_check_device_errors(void *stream) {
-  DeviceState *ds = nullptr;
-  int rc = device_state(&ds);
-  if (rc != EIR_SUCCESS) return rc;
-  cudaStream_t st = static_cast<cudaStream_t>(stream);
-  cudaError_t e = cudaStreamSynchronize(st);
+  // no device state is created here (a caller of eir_contract_no_alloc may
+  // use this without allocating): the words that exist are read and cleared
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return cuda_fail(e, "cudaGetDevice");
+  e = cudaStreamSynchronize(static_cast<cudaStream_t>(stream));
   if (e != cudaSuccess) return cuda_fail(e, "cudaStreamSynchronize");
-  uint32_t h = 0;
-  e = cudaMemcpy(&h, ds->err, sizeof(h), cudaMemcpyDeviceToHost);
-  if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(error word)");
-  if (h != 0) {
-    cudaMemset(ds->err, 0, sizeof(uint32_t));
+  uint32_t *words[2] = {nullptr, eir::noalloc_error_word(dev)};
+  if (dev >= 0 && dev < 64) {
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    words[0] = g_dev[dev].err;
+  }
+  uint32_t code = 0;
+  for (uint32_t *w : words) {
+    if (w == nullptr) continue;
+    uint32_t h = 0;
+    e = cudaMemcpy(&h, w, sizeof(h), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return cuda_fail(e, "cudaMemcpy(error word)");
+    if (h != 0) {
+      e = cudaMemset(w, 0, sizeof(uint32_t));
+      if (e != cudaSuccess) return cuda_fail(e, "cudaMemset(error word)");
+      if (code == 0) code = h;
+    }
+  }
+  if (code != 0) {
     char buf[96];
-    std::snprintf(buf, sizeof(buf), "device wait timed out (code 0x%x)", h);
+    std::snprintf(buf, sizeof(buf), "device wait timed out (code 0x%x)", code);
     return set_error(EIR_DEVICE_TIMEOUT, buf);
   }
   return EIR_SUCCESS;

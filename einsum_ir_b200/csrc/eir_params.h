@@ -51,6 +51,8 @@ struct PermuteParams {
   int32_t mode = 0;        // 0 = copy along the shared stride-1 dim, 1 = 2-D tile transpose
   int32_t vec = 1;         // elements per vector access (copy mode)
   int32_t tdim_in = 0;     // transpose: index of the input's fastest dim
+  int32_t round_tf32 = 0;  // 32-bit elements rounded to the nearest TF32 value as they are copied
+  int32_t pad_ = 0;
   int64_t size[kMaxPermDims] = {};
   int64_t sin[kMaxPermDims] = {};
   int64_t sout[kMaxPermDims] = {};

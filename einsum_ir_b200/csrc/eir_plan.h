@@ -48,6 +48,19 @@ namespace eir {
 cudaError_t api_launch_tc(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
                           TcParams const &tp, void const *aux, void *out, int num_sms,
                           cudaStream_t st);
+// One contraction on `stream` (eir_contract and its variants). ws: the plan's
+// workspace of ws_bytes, or null for the plan's own (allocated on first use);
+// err: the device error word for the bounded waits, or null for the
+// device's own; peers / slab_ctr as for eir_contract_peers / _gather.
+int api_contract(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
+                 PeerOutputs const *peers, void *stream, uint32_t *slab_ctr, void *ws, uint32_t *err,
+                 int num_sms);
+// the workspace bytes a call with these operands uses (0 when it takes the
+// CUDA-core path, which reads the operands in place)
+int64_t api_workspace_needed(eir_plan const *p, void const *l, void const *r);
+// device address of the error word of eir_contract_no_alloc's static scratch
+// on device `dev`, or null before that entry point's first call there
+uint32_t *noalloc_error_word(int dev);
 // a split-K plan (TcParams::split_k > 1): slices into the workspace `ws`,
 // then the reduction into `out` with the plan's touches and peers
 int api_launch_tc_split(eir_plan const *p, CUtensorMap const &ma, CUtensorMap const &mb,
@@ -82,9 +95,13 @@ struct eir_plan {
   std::mutex mu;                 // guards the tensor-map caches
   eir::TensorMapCache cache_a, cache_b;
 
-  // operand pre-permute into the plan's workspace (0 = left, 1 = right, -1 = none)
+  // operand copies into the plan's workspace before the kernel: the operand
+  // whose K walk disagrees is re-laid out (prepack: 0 = left, 1 = right,
+  // -1 = none), and with TF32 compute both operands are rounded to TF32 on
+  // the way; pre_l / pre_r are the copies' permute plans (null: read in place)
   int prepack = -1;
-  eir_plan *pre = nullptr;
+  eir_plan *pre_l = nullptr, *pre_r = nullptr;
+  int64_t ws_off_l = 0, ws_off_r = 0;  // the copies' byte offsets in the workspace
   void *ws = nullptr;
   int64_t ws_bytes = 0;
   int64_t split_ws_offset = 0;  // split-K partial tiles: ws + this offset

@@ -50,16 +50,28 @@ __device__ __forceinline__ void dmma(double &c0, double &c1, double a, double b)
 
 }  // namespace
 
-// Per-thread byte offsets of the DMMA fragments in one stage. A thread reads
-// rows w + x * 8 + g (x = fragment index, g = lane / 4) at k = 4 tq + 2 h + q
-// (tq = lane % 4, h = K half, q = 0, 1); in the 128B swizzle these offsets are a
-// thread constant plus an immediate per x:
+// Per-thread byte offsets of the DMMA fragments in one stage. The sum over the
+// 16 k of a K block is order free, so MMA k-slot tq of K half h and pass q
+// reads the physical k = 2 * pair(h, tq) + q, with pair(0, .) = {0, 2, 5, 7}
+// and pair(1, .) = {1, 3, 4, 6} (A and B use the same map, so every product
+// pairs equal k). A thread reads rows w + x * 8 + g (x = fragment index,
+// g = lane / 4, tq = lane % 4); in the 128B swizzle its offsets are a thread
+// constant plus an immediate per x:
 //  K-major  [rows][16 doubles]: rows are 128 B and the 16-byte chunk index
-//           (k / 2) ^ (row % 8) = (2 tq + h) ^ g does not depend on x, so
+//           (k / 2) ^ (row % 8) = pair ^ g does not depend on x, so
 //           off = base[h] + x * 1024 and one 128-bit load fetches q = 0, 1;
 //  MN-major 8 boxes [16 k][16 rows]: off = box * 2048 + k * 128 + chunk * 16
 //           + (row % 2) * 8 with chunk = ((row % 16) / 2) ^ (k % 8); x moves
 //           the box by x / 2 and flips chunk bit 2 (byte bit 6) by x % 2.
+// The pair map keeps both forms free of shared-memory bank conflicts: in a
+// K-major quarter warp (g = 0 / 1 on rows 128 B apart) the chunks pair ^ 0 and
+// pair ^ 1 are disjoint, and in an MN-major half warp the four tq rows use
+// k % 8 = 2 (pair % 4) + q, distinct in bits 1-2, so the 16 lanes cover 16
+// different 8-byte bank pairs (k = 4 tq + 2 h + q collided tq = 0 with 2).
+__device__ __forceinline__ int dmma_k_pair(int h, int tq) {
+  return h == 0 ? (tq < 2 ? 2 * tq : 2 * tq + 1) : (tq < 2 ? 2 * tq + 1 : 2 * tq);
+}
+
 template <bool MN>
 struct FragOffsets {
   uint32_t base[2][2];  // [h][q]; K-major uses base[h][0] only
@@ -68,11 +80,12 @@ struct FragOffsets {
     for (int h = 0; h < 2; ++h)
 #pragma unroll
       for (int q = 0; q < 2; ++q) {
-        const int k = 4 * tq + 2 * h + q;
+        const int pair = dmma_k_pair(h, tq);
+        const int k = 2 * pair + q;
         if (MN)
           base[h][q] = (uint32_t)((w >> 4) * 2048 + k * 128 + ((((g >> 1) ^ (k & 7))) << 4) + ((g & 1) << 3));
         else
-          base[h][q] = (uint32_t)((w + g) * 128 + (((2 * tq + h) ^ g) << 4));
+          base[h][q] = (uint32_t)((w + g) * 128 + ((pair ^ g) << 4));
       }
   }
   // the pair (k, k + 1) of fragment x in K half h
@@ -191,8 +204,8 @@ __global__ void __launch_bounds__(kDmmaThreads, 1)
         }
         const uint8_t *tA = sA + stage * kDmmaTileBytes, *tB = sB + stage * kDmmaTileBytes;
         // The sum over the block's 16 k is order free: MMA k-slot tq takes the
-        // physical k = 4 tq + 2 h + q over the four MMAs (h, q), so a thread's
-        // values for q = 0, 1 share one 16-byte chunk of a K-major tile.
+        // physical k = 2 dmma_k_pair(h, tq) + q over the four MMAs (h, q), so a
+        // thread's values for q = 0, 1 share one 16-byte chunk of a K-major tile.
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           double2 a[WI], b[WJ];

@@ -235,9 +235,24 @@ cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const 
 }
 
 // ------------------------------------------------------------------ permute
+// an element as copied by a permute: FP32 words rounded to the nearest TF32
+// value when the permute feeds a TF32 contraction (PermuteParams::round_tf32)
+template <typename T>
+__device__ __forceinline__ T copy_elem(T x, int32_t round_tf32) {
+  return x;
+}
+template <>
+__device__ __forceinline__ uint32_t copy_elem<uint32_t>(uint32_t x, int32_t round_tf32) {
+  return round_tf32 ? round_tf32_bits(x) : x;
+}
+
 // copy mode: dim 0 is stride-1 in input and output; V elements per access.
-// ZERO: the unary ZERO primitive (out = 0 over the output's strides; `in` unused)
-template <typename T, int V, bool ZERO>
+// ZERO: the unary ZERO primitive (out = 0 over the output's strides; `in` unused).
+// I: index type, int32_t whenever every element offset of both tensors fits.
+// A copy whose dims all fused into one (nd == 1: a contiguous or uniformly
+// strided run, e.g. the TF32-rounding copy of an operand) skips the index
+// decomposition and keeps 4 independent vectors in flight per thread.
+template <typename T, int V, bool ZERO, typename I>
 __global__ void __launch_bounds__(256)
     permute_copy_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
   struct alignas(sizeof(T) * V) Vec {
@@ -245,39 +260,84 @@ __global__ void __launch_bounds__(256)
   };
   pdl_launch_dependents();
   pdl_wait();
-  const int64_t n0v = p.size[0] / V;
-  const int64_t total = p.rows * n0v;
-  for (int64_t g = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; g < total;
-       g += (int64_t)gridDim.x * blockDim.x) {
-    int64_t i0 = g % n0v;
-    int64_t row = g / n0v;
-    int64_t oi = 0, oo = 0;
+  const I n0v = (I)(p.size[0] / V);
+  const I total = (I)p.rows * n0v;
+  const I nthr = (I)gridDim.x * (I)blockDim.x;
+  const I tid = (I)blockIdx.x * (I)blockDim.x + (I)threadIdx.x;
+  if (p.nd == 1) {
+    const I sin0 = (I)p.sin[0], sout0 = (I)p.sout[0];
+    for (I g = tid; g < total; g += 4 * nthr) {
+      Vec v[4];
 #pragma unroll
-    for (int d = 1; d < kMaxPermDims; ++d) {
-      if (d < p.nd) {
-        int64_t i = row % p.size[d];
-        row /= p.size[d];
-        oi += i * p.sin[d];
-        oo += i * p.sout[d];
+      for (int j = 0; j < 4; ++j) {
+        const I e = g + (I)j * nthr;
+        if (!ZERO && e < total) v[j] = *reinterpret_cast<Vec const *>(in + e * V * sin0);
+      }
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const I e = g + (I)j * nthr;
+        if (e >= total) continue;
+        if (ZERO) {
+          *reinterpret_cast<Vec *>(out + e * V * sout0) = Vec{};
+        } else {
+#pragma unroll
+          for (int k = 0; k < V; ++k) v[j].v[k] = copy_elem(v[j].v[k], p.round_tf32);
+          *reinterpret_cast<Vec *>(out + e * V * sout0) = v[j];
+        }
       }
     }
-    // V > 1 only when dim 0 has unit stride on both sides (checked by the planner)
-    if (ZERO) {
-      *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) = Vec{};
-    } else {
-      *reinterpret_cast<Vec *>(out + oo + i0 * V * p.sout[0]) =
-          *reinterpret_cast<Vec const *>(in + oi + i0 * V * p.sin[0]);
+    return;
+  }
+  // general: 4 vectors per thread and iteration, each decomposed into its row
+  // offsets (V > 1 only when dim 0 has unit stride on both sides, checked by
+  // the planner)
+  for (I g = tid; g < total; g += 4 * nthr) {
+    I src[4], dst[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const I e = g + (I)j * nthr;
+      I i0 = e % n0v, row = e / n0v;
+      I oi = i0 * V * (I)p.sin[0], oo = i0 * V * (I)p.sout[0];
+#pragma unroll
+      for (int d = 1; d < kMaxPermDims; ++d) {
+        if (d < p.nd) {
+          I i = row % (I)p.size[d];
+          row /= (I)p.size[d];
+          oi += i * (I)p.sin[d];
+          oo += i * (I)p.sout[d];
+        }
+      }
+      src[j] = oi;
+      dst[j] = oo;
+    }
+    Vec v[4];
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      if (!ZERO && g + (I)j * nthr < total) v[j] = *reinterpret_cast<Vec const *>(in + src[j]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      if (g + (I)j * nthr >= total) continue;
+      if (ZERO) {
+        *reinterpret_cast<Vec *>(out + dst[j]) = Vec{};
+      } else {
+#pragma unroll
+        for (int k = 0; k < V; ++k) v[j].v[k] = copy_elem(v[j].v[k], p.round_tf32);
+        *reinterpret_cast<Vec *>(out + dst[j]) = v[j];
+      }
     }
   }
 }
 
 // transpose mode: dim 0 is the output's stride-1 dim, dim tdim_in the input's.
-// I: index type, int32_t whenever every element offset of both tensors fits
-// (the common case; 64-bit divisions in the tile decode cost ~1 us per tile).
+// 64 x 64 tiles through shared memory (padded rows: conflict-free both ways),
+// 16 elements per thread in flight on each side, so the copy is not latency
+// bound. I: index type, int32_t whenever every element offset of both tensors
+// fits (the common case; 64-bit divisions in the tile decode are slow).
+constexpr int kTransposeTile = 64;
 template <typename T, typename I>
 __global__ void __launch_bounds__(256)
     permute_transpose_kernel(const PermuteParams p, const T *__restrict__ in, T *__restrict__ out) {
-  constexpr int TS = 32;
+  constexpr int TS = kTransposeTile;
   __shared__ T tile[TS][TS + 1];
   const int tx = threadIdx.x & 31, ty = threadIdx.x >> 5;  // 32 x 8
   const int td = p.tdim_in;
@@ -288,9 +348,12 @@ __global__ void __launch_bounds__(256)
   const I nblk = t0 * tt * (I)p.batch;
   const I sin0 = (I)p.sin[0], sint = (I)p.sin[td], sout0 = (I)p.sout[0], soutt = (I)p.sout[td];
   for (I blk = (I)blockIdx.x; blk < nblk; blk += (I)gridDim.x) {
+    // diagonal order: blocks running at the same time cover different tiles
+    // along both dims, not one band of columns of the input (which maps to few
+    // DRAM channels); b0 -> bt is a rotation, so every tile is visited once
     const I b0 = blk % t0;
     const I r = blk / t0;
-    const I bt = r % tt;
+    const I bt = (r % tt + b0) % tt;
     I bat = r / tt;
     I oi = 0, oo = 0;
 #pragma unroll
@@ -302,19 +365,24 @@ __global__ void __launch_bounds__(256)
         oo += i * (I)p.sout[d];
       }
     }
-    // load: consecutive threads walk the input's stride-1 dim
+    // load: consecutive threads walk the input's stride-1 dim (2 x 32 columns)
 #pragma unroll
-    for (int i = 0; i < TS / 8; ++i) {
-      const I it = bt * TS + tx, i0 = b0 * TS + ty + 8 * i;
-      if (it < st && i0 < s0) tile[ty + 8 * i][tx] = in[oi + it * sint + i0 * sin0];
-    }
+    for (int i = 0; i < TS / 8; ++i)
+#pragma unroll
+      for (int c = 0; c < TS / 32; ++c) {
+        const I it = bt * TS + tx + 32 * c, i0 = b0 * TS + ty + 8 * i;
+        if (it < st && i0 < s0)
+          tile[ty + 8 * i][tx + 32 * c] = copy_elem(in[oi + it * sint + i0 * sin0], p.round_tf32);
+      }
     __syncthreads();
     // store: consecutive threads walk the output's stride-1 dim
 #pragma unroll
-    for (int i = 0; i < TS / 8; ++i) {
-      const I i0 = b0 * TS + tx, it = bt * TS + ty + 8 * i;
-      if (it < st && i0 < s0) out[oo + i0 * sout0 + it * soutt] = tile[tx][ty + 8 * i];
-    }
+    for (int i = 0; i < TS / 8; ++i)
+#pragma unroll
+      for (int c = 0; c < TS / 32; ++c) {
+        const I i0 = b0 * TS + tx + 32 * c, it = bt * TS + ty + 8 * i;
+        if (it < st && i0 < s0) out[oo + i0 * sout0 + it * soutt] = tile[tx + 32 * c][ty + 8 * i];
+      }
     __syncthreads();
   }
 }
@@ -375,13 +443,14 @@ cudaError_t launch_cpx_expand(int esize, PermuteParams const &p, int64_t cpx_str
   return cudaErrorInvalidValue;
 }
 
-template <typename T, bool ZERO>
+template <typename T, bool ZERO, typename I>
 static cudaError_t launch_copy_t(PermuteParams const &p, T const *i, T *o, int64_t blocks, cudaStream_t st) {
+  const dim3 g((unsigned)blocks), b(256);
   switch (p.vec) {
-    case 1: return launch_kernel(permute_copy_kernel<T, 1, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
-    case 2: return launch_kernel(permute_copy_kernel<T, 2, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
-    case 4: return launch_kernel(permute_copy_kernel<T, 4, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
-    case 8: return launch_kernel(permute_copy_kernel<T, 8, ZERO>, dim3((unsigned)blocks), dim3(256), 0, st, p, i, o);
+    case 1: return launch_kernel(permute_copy_kernel<T, 1, ZERO, I>, g, b, 0, st, p, i, o);
+    case 2: return launch_kernel(permute_copy_kernel<T, 2, ZERO, I>, g, b, 0, st, p, i, o);
+    case 4: return launch_kernel(permute_copy_kernel<T, 4, ZERO, I>, g, b, 0, st, p, i, o);
+    case 8: return launch_kernel(permute_copy_kernel<T, 8, ZERO, I>, g, b, 0, st, p, i, o);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -400,10 +469,16 @@ static cudaError_t launch_permute_t(PermuteParams const &p, void const *in, void
     int64_t cap = (int64_t)num_sms * 16;
     if (blocks > cap) blocks = cap;
     if (blocks < 1) blocks = 1;
-    e = zero ? launch_copy_t<T, true>(p, i, o, blocks, st) : launch_copy_t<T, false>(p, i, o, blocks, st);
+    if (offsets_fit_int32(p))
+      e = zero ? launch_copy_t<T, true, int32_t>(p, i, o, blocks, st)
+               : launch_copy_t<T, false, int32_t>(p, i, o, blocks, st);
+    else
+      e = zero ? launch_copy_t<T, true, int64_t>(p, i, o, blocks, st)
+               : launch_copy_t<T, false, int64_t>(p, i, o, blocks, st);
   } else {
-    int64_t nblk = ((p.size[0] + 31) / 32) * ((p.size[p.tdim_in] + 31) / 32) * p.batch;
-    int64_t cap = (int64_t)num_sms * 8;  // 8 x 256 threads fill an SM: the copy is latency bound
+    const int64_t ts = kTransposeTile;
+    int64_t nblk = ((p.size[0] + ts - 1) / ts) * ((p.size[p.tdim_in] + ts - 1) / ts) * p.batch;
+    int64_t cap = (int64_t)num_sms * 8;  // 8 x 256 threads per SM
     int64_t blocks = nblk < cap ? nblk : cap;
     if (blocks < 1) blocks = 1;
     if (offsets_fit_int32(p))

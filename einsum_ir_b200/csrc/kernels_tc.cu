@@ -18,11 +18,11 @@
 // Warp roles: warp 0 = TMA producer, warp 1 = MMA issuer (+TMEM owner),
 // warps 2..5 = epilogue (TMEM -> registers -> global, fused first/last touch:
 // ZERO/COPY/ADD before, RELU/ADD after, aux read through broadcast strides),
-// warps 6..9 (TF32 and 3xTF32) = converters: TF32 rounds each staged FP32
-// tile in place to the nearest TF32 value (round_tf32_inplace); 3xTF32 stores
-// lo = x - trunc_TF32(x) of each staged tile next to it in shared memory (the
-// staged x is the hi part, see split_tf32_lo) so three MMAs (lo*hi + hi*lo +
-// hi*hi) give an FP32-accurate product.
+// warps 6..9 (3xTF32 only) = converters (split_stage): store
+// lo = x - trunc_TF32(x) of each staged FP32 tile next to it in shared memory
+// (the staged x is the hi part, see tf32_lo_bits) so three MMAs (lo*hi + hi*lo
+// + hi*hi) give an FP32-accurate product. TF32 plans read operand copies that
+// the planner's copy kernels have already rounded to the nearest TF32 value.
 //
 // Semantics follow the reference loop engine: first touch at the first K
 // step, last touch after the last (ContractionBackend.cpp:296-348,495-515;
@@ -48,8 +48,7 @@ struct TcConfig {
   static constexpr int kABytes = KSUB * kASub;             // per stage
   static constexpr int kBBytes = KSUB * kBSub;
   static constexpr bool kSplit = (KIND == kKind3xTF32);
-  static constexpr bool kRound = (KIND == kKindTF32);      // round staged tiles to TF32 in place
-  static constexpr bool kConv = kSplit || kRound;          // converter warps 6..9
+  static constexpr bool kConv = kSplit;                    // converter warps 6..9
   static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
   static constexpr int kStages = 196608 / kStageBytes;
   static constexpr int kThreads = kConv ? 320 : 192;
@@ -313,7 +312,7 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
       if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else if (Cfg::kConv) {
+  } else if constexpr (Cfg::kConv) {
     // ------------------------------------------------------------ converters
     const int ct = threadIdx.x - 192;  // 0..127
     int stage = 0;
@@ -326,21 +325,10 @@ __global__ void __launch_bounds__(TcConfig<KIND, BN, KSUB>::kThreads, 1)
           ok = false;
           break;
         }
-        float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
-        float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
-        if (Cfg::kSplit) {
-          float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kABytes / 16; i += 128) split_tf32_lo(&a[i], &alo[i]);
-          float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kBBytes / 16; i += 128) split_tf32_lo(&b[i], &blo[i]);
-        } else {
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kABytes / 16; i += 128) round_tf32_inplace(&a[i]);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kBBytes / 16; i += 128) round_tf32_inplace(&b[i]);
-        }
+        const uint32_t a = smem_u32(sA + stage * Cfg::kABytes);
+        const uint32_t b = smem_u32(sB + stage * Cfg::kBBytes);
+        split_stage<Cfg::kABytes, 128>(a, smem_u32(sAlo + stage * Cfg::kABytes), ct);
+        split_stage<Cfg::kBBytes, 128>(b, smem_u32(sBlo + stage * Cfg::kBBytes), ct);
         fence_proxy_async_smem();
         mbar_arrive(&conv[stage]);
         if (++stage == S) {

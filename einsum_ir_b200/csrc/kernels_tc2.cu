@@ -18,13 +18,13 @@
 // Warp roles per CTA: warp 0 = TMA producer, warp 1 = MMA issuer (leader) and
 // TMEM owner (both CTAs allocate with cta_group::2), warps 2..9 = epilogue, two
 // per TMEM lane quadrant with half of the columns each (fused first / last
-// touch as in the one-CTA kernel). TF32 and FP32-exact (3xTF32) modes: warps
-// 2..5 = epilogue, warps 6..9 = converters, which round each CTA's staged FP32
-// tiles in place to the nearest TF32 value (TF32) or split them into hi / lo
-// TF32 parts (3xTF32); the loads of a CTA then complete on its own barrier
-// and the MMA issuer waits for the converter warps of both CTAs. Every wait
-// is bounded; a timeout raises the abort flag in both CTAs and records a
-// device error.
+// touch as in the one-CTA kernel). FP32-exact mode (3xTF32): warps 2..5 =
+// epilogue, warps 6..9 split each CTA's staged FP32 tiles into hi / lo TF32
+// parts; the loads of a CTA then complete on its own barrier and the MMA
+// issuer waits for the converter warps of both CTAs. TF32 plans read operand
+// copies that the planner's copy kernels have already rounded to the nearest
+// TF32 value. Every wait is bounded; a timeout raises the abort flag in both
+// CTAs and records a device error.
 #include <cuda.h>
 #include "eir_common.cuh"
 #include "eir_params.h"
@@ -48,14 +48,13 @@ struct PairConfig {
   static constexpr int kBBytes = KSUB * kBSub;
   // FP32-exact mode keeps a hi and a lo TF32 copy of every staged operand
   static constexpr bool kSplit = (KIND == kKind3xTF32);
-  static constexpr bool kRound = (KIND == kKindTF32);  // round staged tiles to TF32 in place
-  static constexpr bool kConv = kSplit || kRound;      // converter warps
+  static constexpr bool kConv = kSplit;                // converter warps (hi / lo split)
   static constexpr int kStageBytes = (kABytes + kBBytes) * (kSplit ? 2 : 1);
   static constexpr int kMaxStages = 8;
   static constexpr int kFit = (232448 - 1024 - 512) / kStageBytes;
   static constexpr int kStages = kFit < kMaxStages ? kFit : kMaxStages;
   // epilogue: 2 warps per TMEM lane quadrant (half the columns each), or 1
-  // next to the 4 converter warps of the TF32 / FP32-exact modes
+  // next to the 4 converter warps of the FP32-exact mode
   static constexpr int kEpiWarps = kConv ? 4 : 8;
   static constexpr int kConvWarps = kConv ? 4 : 0;
   static constexpr int kThreads = 32 * (2 + kEpiWarps + kConvWarps);
@@ -347,11 +346,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
       if (acc == 0) acc_phase ^= 1u;
       }
     }
-  } else if (Cfg::kConv) {
+  } else if constexpr (Cfg::kConv) {
     // ------------------------------------------------------------ converters (both CTAs)
-    // each CTA rounds or splits its own staged halves, then every converter
-    // warp of the pair arrives on the leader's conv barrier, which the MMA
-    // issuer waits on
+    // each CTA splits its own staged halves, then every converter warp of
+    // the pair arrives on the leader's conv barrier, which the MMA issuer
+    // waits on
     const int ct = threadIdx.x - 32 * (2 + Cfg::kEpiWarps);  // 0 .. 32 * kConvWarps - 1
     constexpr int kCt = 32 * Cfg::kConvWarps;
     const uint32_t conv_leader = mapa_shared(smem_u32(conv), 0);
@@ -364,21 +363,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(PairConfig<KIND, BN,
           ok = false;
           break;
         }
-        float4 *a = reinterpret_cast<float4 *>(sA + stage * Cfg::kABytes);
-        float4 *b = reinterpret_cast<float4 *>(sB + stage * Cfg::kBBytes);
-        if (Cfg::kSplit) {
-          float4 *alo = reinterpret_cast<float4 *>(sAlo + stage * Cfg::kABytes);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kABytes / 16; i += kCt) split_tf32_lo(&a[i], &alo[i]);
-          float4 *blo = reinterpret_cast<float4 *>(sBlo + stage * Cfg::kBBytes);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) split_tf32_lo(&b[i], &blo[i]);
-        } else {
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kABytes / 16; i += kCt) round_tf32_inplace(&a[i]);
-#pragma unroll 4
-          for (int i = ct; i < Cfg::kBBytes / 16; i += kCt) round_tf32_inplace(&b[i]);
-        }
+        const uint32_t a = smem_u32(sA + stage * Cfg::kABytes);
+        const uint32_t b = smem_u32(sB + stage * Cfg::kBBytes);
+        split_stage<Cfg::kABytes, kCt>(a, smem_u32(sAlo + stage * Cfg::kABytes), ct);
+        split_stage<Cfg::kBBytes, kCt>(b, smem_u32(sBlo + stage * Cfg::kBBytes), ct);
         fence_proxy_async_smem();  // the tensor cores read these tiles
         __syncwarp();
         if ((threadIdx.x & 31) == 0) mbar_arrive_cluster(conv_leader + 8u * (uint32_t)stage);

@@ -183,22 +183,36 @@ __device__ __forceinline__ ProducerTile producer_tile(TcParams const &p, int64_t
 // reads a TF32 operand from an FP32 word by ignoring its 13 low mantissa bits,
 // so the staged x already is hi: only lo has to be computed and stored. The
 // FP32 parity tests (relative error ~1e-6 against the oracle) pin this.
-__device__ __forceinline__ void split_tf32_lo(float4 const *x_in, float4 *lo_out) {
-  const float4 x = *x_in;
-  auto lo = [](float v) { return v - __uint_as_float(__float_as_uint(v) & 0xFFFFE000u); };
-  *lo_out = make_float4(lo(x.x), lo(x.y), lo(x.z), lo(x.w));
+__device__ __forceinline__ uint32_t tf32_lo_bits(uint32_t u) {
+  const float v = __uint_as_float(u);
+  return __float_as_uint(v - __uint_as_float(u & 0xFFFFE000u));
 }
 
-// TF32 mode: each staged FP32 operand is rounded in place to the nearest TF32
-// value (round_tf32_bits) before the tensor core reads it, which would
-// otherwise ignore the 13 low mantissa bits (truncation).
-__device__ __forceinline__ void round_tf32_inplace(float4 *x_io) {
-  uint4 u = *reinterpret_cast<uint4 *>(x_io);
-  u.x = round_tf32_bits(u.x);
-  u.y = round_tf32_bits(u.y);
-  u.z = round_tf32_bits(u.z);
-  u.w = round_tf32_bits(u.w);
-  *reinterpret_cast<uint4 *>(x_io) = u;
+// hi / lo split of one staged FP32 operand of BYTES at shared address `src`:
+// lo(x) is stored at the same offset from `dst`. Thread `t` of NT handles
+// 16-byte chunks t, t + NT, ... in batches of 8 independent loads, so the
+// shared-memory latency overlaps instead of adding up per chunk.
+template <int BYTES, int NT>
+__device__ __forceinline__ void split_stage(uint32_t src, uint32_t dst, int t) {
+  constexpr int kChunks = BYTES / 16 / NT;  // 16-byte chunks per thread
+  static_assert(BYTES % (16 * NT) == 0, "whole chunks per thread");
+  constexpr int kBatch = kChunks < 8 ? kChunks : 8;
+  static_assert(kChunks % kBatch == 0, "whole batches");
+#pragma unroll
+  for (int b = 0; b < kChunks; b += kBatch) {
+    uint4 v[kBatch];
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) v[j] = lds128(src + (uint32_t)(((b + j) * NT + t) * 16));
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) {
+      v[j].x = tf32_lo_bits(v[j].x);
+      v[j].y = tf32_lo_bits(v[j].y);
+      v[j].z = tf32_lo_bits(v[j].z);
+      v[j].w = tf32_lo_bits(v[j].w);
+    }
+#pragma unroll
+    for (int j = 0; j < kBatch; ++j) sts128(dst + (uint32_t)(((b + j) * NT + t) * 16), v[j]);
+  }
 }
 
 // Epilogue variant of a plan: 0 = ZERO first touch and no last touch, 1 = COPY
