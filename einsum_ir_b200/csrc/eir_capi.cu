@@ -982,6 +982,30 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   p->num_ops = 2 * sc * sm * sn * sk;
   if (p->first == EIR_KTYPE_ZERO) p->num_ops -= sc * sm * sn;
 
+  // Operand roles (the reference's swap_inputs rule, BinaryPrimitives.cpp:87-134):
+  // the output's unit-stride dim should be an M dim. The tensor-core epilogues
+  // hold one output row per thread (TMEM lane) and store a column of 32 rows
+  // per warp instruction, which coalesces only along M; with the output
+  // contiguous along N every lane would write its own row segment. So when the
+  // output's fastest dim is an N dim, left and right change roles (M <-> N);
+  // the products, hence the result, are the same.
+  {
+    int fastest = -1;
+    for (int i = 0; i < (int)dims.size(); ++i)
+      if (dims[i].type != EIR_DIM_K && dims[i].size > 1 && dims[i].so != 0 &&
+          (fastest < 0 || std::llabs(dims[i].so) < std::llabs(dims[fastest].so)))
+        fastest = i;
+    if (fastest >= 0 && dims[fastest].type == EIR_DIM_N && sm > 1) {
+      p->swapped = true;
+      for (auto &x : dims) {
+        if (x.type == EIR_DIM_M) x.type = EIR_DIM_N;
+        else if (x.type == EIR_DIM_N) x.type = EIR_DIM_M;
+        std::swap(x.sl, x.sr);
+      }
+      std::swap(p->dt_l, p->dt_r);
+    }
+  }
+
   p->dims = simplify_dims(dims);
   for (int ty = EIR_DIM_C; ty <= EIR_DIM_K; ++ty) {
     eir::GroupDims *g = ty == EIR_DIM_C ? &p->simt.c : ty == EIR_DIM_M ? &p->simt.m
@@ -1013,6 +1037,7 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   }
   const bool tensor_cores = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
   p->text = (tensor_cores ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
+  if (p->swapped) p->text += "| operands swapped (output contiguous along the right operand) ";
   if (p->out_dense)
     p->text += "| gather: " + std::to_string(p->slab_count) + " slab(s)" +
                (p->slab_counted ? ", counted by the kernel" : ", released after the kernel");
@@ -1056,6 +1081,7 @@ int contract_impl(eir_plan *p, void const *l, void const *r, void const *aux, vo
     return set_error(EIR_NO_DATA_PTR_PROVIDED, "null operand pointer");
   bool uses_aux = p->first == EIR_KTYPE_COPY || p->first == EIR_KTYPE_ADD || p->last == EIR_KTYPE_ADD;
   if (uses_aux && aux == nullptr) return set_error(EIR_NO_DATA_PTR_PROVIDED, "null aux pointer");
+  if (p->swapped) std::swap(l, r);  // the plan's left operand is the caller's right one
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (p->cpx_inner != nullptr) {
     if (ws_ext != nullptr) return set_error(EIR_INVALID_ARGUMENT, "complex plans need their own workspace");

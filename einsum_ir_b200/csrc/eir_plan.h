@@ -78,6 +78,7 @@ struct eir_plan {
   int dt_l = 0, dt_r = 0, dt_o = 0, comp = 0, first = 99, last = 99;
   int desc_flags = 0;
   bool empty = false;            // nothing to compute (a C/M/N dim of size 0)
+  bool swapped = false;          // left and right change roles (dims and dt_l / dt_r are the swapped ones)
   std::vector<eir::LDim> dims;   // after size-1 removal and fusion
   eir::SimtParams simt;
   bool tc = false;

@@ -231,6 +231,28 @@ def test_simt_tf32_general_inputs(cuda):
              expect_family=SIMT, tc_min_ops=str(1 << 40))
 
 
+@pytest.mark.parametrize("expr,sizes,dtype", [
+    ("mk,nk->mn", dict(m=256, n=384, k=192), "bf16"),
+    ("mk,kn->mn", dict(m=256, n=384, k=96), "fp32"),
+    ("km,kn->mn", dict(m=200, n=130, k=64), "tf32"),
+    ("zabcd,zcdef->zabef", dict(z=3, a=8, b=8, c=8, d=8, e=8, f=8), "fp32"),
+    ("zabcd,zcdef->zabef", dict(z=3, a=8, b=8, c=8, d=8, e=8, f=8), "fp64"),
+])
+def test_tc_output_contiguous_along_right_operand(cuda, expr, sizes, dtype):
+    # the output's unit-stride dim belongs to the right operand: the plan swaps
+    # the operand roles (the reference's swap_inputs rule) and the result stays
+    plan, _ = run_case(cuda, expr, sizes, dtype)
+    assert "operands swapped" in plan.describe(), plan.describe()
+
+
+@pytest.mark.parametrize("dtype", ["fp32", "bf16", "fp64"])
+def test_swapped_mlp_layer_bias_relu(cuda, dtype):
+    # bi,io->bo: bias broadcast over b, output contiguous along o (right operand)
+    plan, _ = run_case(cuda, "bi,io->bo", dict(b=256, i=192, o=320), dtype, first=cabi.KTYPE_COPY,
+                       last=cabi.KTYPE_RELU, aux_outer="b")
+    assert "operands swapped" in plan.describe(), plan.describe()
+
+
 @pytest.mark.parametrize("dtype", ["fp32", "bf16", "tf32"])
 @pytest.mark.parametrize("pair", [0, 1])
 def test_tc_mlp_layer_bias_relu(cuda, dtype, pair):
