@@ -8,7 +8,8 @@
 // Data as the reference driver: left uniform [0, 1), right ones (:57-59).
 // Timing: repeated contract() calls for ~0.5 s with CUDA events. Check: the
 // same contraction in FP64 on the CUDA-core kernel, relative Frobenius error
-// (the reference uses at::allclose with 1e-3, :155).
+// (the reference uses at::allclose with 1e-3, :155); with EIR_DRIVER_DUMP=<dir>
+// the inputs and the result are also written for the CPU oracle.
 #include <cuda_runtime.h>
 #include <chrono>
 #include <cstdio>
@@ -170,6 +171,15 @@ int main(int argc, char *argv[]) {
 
   // check against the FP64 CUDA-core contraction of the same values
   std::vector<double> got = download(dout);
+  {
+    Dump dump;  // EIR_DRIVER_DUMP: inputs and result for the CPU oracle
+    dump.line("expr", expr_arg);
+    dump.line("sizes", sizes_arg);
+    dump.line("dtype", dtype);
+    dump.tensor("in0", ids[0], shape[0], hl);
+    dump.tensor("in1", ids[1], shape[1], hr);
+    dump.tensor("out", ids[2], shape[2], got);
+  }
   DeviceTensor rl, rr, rout;
   upload(hl, 8, rl);
   upload(hr, 8, rr);

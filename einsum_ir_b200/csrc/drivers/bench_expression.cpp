@@ -14,7 +14,9 @@
 // reference times one eval with a host clock); the check solution is the
 // same tree in FP64 on the CUDA-core kernels (the reference compares with
 // at::einsum, src/bench_expression.cpp:380-541), with the reference's
-// tolerances 1e-5 (FP32, BF16) and 1e-12 (FP64), 1e-2 for TF32.
+// tolerances 1e-5 (FP32, BF16) and 1e-12 (FP64), 1e-2 for TF32. With
+// EIR_DRIVER_DUMP=<dir> the inputs and the result are also written for the
+// CPU oracle (see driver_util.h), which the tests compare against.
 #include <cuda_runtime.h>
 #include <chrono>
 #include <cstdio>
@@ -248,6 +250,21 @@ int main(int argc, char *argv[]) {
 
   // ---- check: the same tree in FP64 on the CUDA-core kernels, same input values
   std::vector<double> got = download(dev.back());
+  {
+    Dump dump;  // EIR_DRIVER_DUMP: inputs and result for the CPU oracle
+    dump.line("expr", expr_arg);
+    dump.line("sizes", sizes_arg);
+    dump.line("path", path_arg);
+    dump.line("dtype", dtype);
+    for (int64_t t = 0; t < tr.num_tensors; ++t) {
+      std::vector<int64_t> tids;
+      int64_t off = 0;
+      for (int64_t u = 0; u < t; ++u) off += tr.string_num_dims[u];
+      for (int64_t d = 0; d < tr.string_num_dims[t]; ++d) tids.push_back(tr.string_dim_ids[off + d]);
+      const bool is_out = t + 1 == tr.num_tensors;
+      dump.tensor(is_out ? "out" : "in" + std::to_string(t), tids, tr.shapes[t], is_out ? got : held[t]);
+    }
+  }
   std::vector<DeviceTensor> ref_dev(tr.num_tensors);
   std::vector<void *> ref_ptrs(tr.num_tensors);
   for (int64_t t = 0; t < tr.num_tensors; ++t) {

@@ -6,7 +6,9 @@
 //   bench_tree einsum_tree dimension_sizes [dtype]
 // dtype: FP32 (default), FP64, BF16 (BF16 leaves, FP32 inner nodes and output)
 // or TF32. Data: seeded uniform [-1, 1) leaves (the reference draws
-// at::randn); eval time: mean of a CUDA-event-timed loop.
+// at::randn); eval time: mean of a CUDA-event-timed loop. With
+// EIR_DRIVER_DUMP=<dir> the parsed tree, the leaves and the result are also
+// written for the CPU oracle (see driver_util.h).
 #include <cuda_runtime.h>
 #include <chrono>
 #include <cstdio>
@@ -121,6 +123,24 @@ int main(int argc, char *argv[]) {
               sizes_arg.c_str(), (long long)flops, t_compile, t_eval, gf_eval, gf_total);
 
   std::vector<double> got = download(dev[n - 1]), ref;
+  {
+    Dump dump;  // EIR_DRIVER_DUMP: the parsed tree, its leaves and the result for the CPU oracle
+    dump.line("tree", tree_arg);
+    dump.line("sizes", sizes_arg);
+    dump.line("dtype", dtype);
+    for (int64_t i = 0; i < n; ++i) {
+      std::string ch;
+      for (size_t c = 0; c < children[i].size(); ++c) ch += (c ? "," : "") + std::to_string(children[i][c]);
+      std::string ids_s;
+      for (size_t d = 0; d < ids[i].size(); ++d) ids_s += (d ? "," : "") + std::to_string(ids[i][d]);
+      dump.line("node" + std::to_string(i),
+                "ids " + (ids_s.empty() ? "-" : ids_s) + " children " + (ch.empty() ? "-" : ch));
+      std::vector<int64_t> shp;
+      for (auto d : ids[i]) shp.push_back(sizes[d]);
+      if (i + 1 == n) dump.tensor("out", ids[i], shp, got);
+      else if (children[i].empty()) dump.tensor("leaf" + std::to_string(i), ids[i], shp, download(ref_dev[i]));
+    }
+  }
   {
     CudaCoreOnly guard;
     EinsumTree ref_tree;

@@ -168,6 +168,51 @@ inline void print_report(ErrorReport const &r, char const *ref_name) {
   std::printf("  relative error:                               %g\n", r.rel);
 }
 
+// EIR_DRIVER_DUMP=<dir>: a driver writes the values its input tensors hold
+// (<name>.f64, float64, the tensor's own layout), its result (out.f64) and a
+// manifest (manifest.txt: one "key value..." line per fact: the command's
+// arguments, each tensor's dimension ids and sizes, tree nodes), so that a
+// test can recompute the result with the CPU oracle on the same values.
+struct Dump {
+  std::string dir;
+  FILE *manifest = nullptr;
+  Dump() {
+    char const *v = std::getenv("EIR_DRIVER_DUMP");
+    if (v == nullptr || *v == 0) return;
+    dir = v;
+    manifest = std::fopen((dir + "/manifest.txt").c_str(), "w");
+    if (manifest == nullptr) {
+      std::fprintf(stderr, "error: cannot write %s/manifest.txt\n", dir.c_str());
+      std::exit(EXIT_FAILURE);
+    }
+  }
+  ~Dump() {
+    if (manifest) std::fclose(manifest);
+  }
+  bool on() const { return manifest != nullptr; }
+  void line(std::string const &key, std::string const &value) {
+    if (on()) std::fprintf(manifest, "%s %s\n", key.c_str(), value.c_str());
+  }
+  // "<name> ids i,j,... sizes a,b,..." and the values as <name>.f64
+  void tensor(std::string const &name, std::vector<int64_t> const &ids, std::vector<int64_t> const &sizes,
+              std::vector<double> const &values) {
+    if (!on()) return;
+    std::string s = "ids ";
+    for (size_t i = 0; i < ids.size(); ++i) s += (i ? "," : "") + std::to_string(ids[i]);
+    if (ids.empty()) s += "-";
+    s += " sizes ";
+    for (size_t i = 0; i < sizes.size(); ++i) s += (i ? "," : "") + std::to_string(sizes[i]);
+    if (sizes.empty()) s += "-";
+    line(name, s);
+    FILE *f = std::fopen((dir + "/" + name + ".f64").c_str(), "wb");
+    if (f == nullptr || std::fwrite(values.data(), sizeof(double), values.size(), f) != values.size()) {
+      std::fprintf(stderr, "error: cannot write %s/%s.f64\n", dir.c_str(), name.c_str());
+      std::exit(EXIT_FAILURE);
+    }
+    std::fclose(f);
+  }
+};
+
 // Plans created while this guard lives run on the CUDA-core kernels only (the
 // planner's tensor-core size threshold is raised out of reach): the drivers'
 // FP64 reference solution.

@@ -113,8 +113,10 @@ def driver_command(mode: int, args: list, dtype: str) -> list:
 
 
 def run(samples: Path, keys: list, mode: int, reps: int, dtype: str, log_dir: Path,
-        dry_run: bool = False, timeout: float = 600.0, max_per_key: int = 0) -> list:
-    table = settings_for(mode)
+        dry_run: bool = False, timeout: float = 600.0, max_per_key: int = 0, table: dict | None = None) -> list:
+    """runs the settings of `keys`; `table` maps keys to setting files under
+    `samples` (default: the reference's suite layout, settings_for(mode))"""
+    table = settings_for(mode) if table is None else table
     rows = []
     for key in keys:
         if key not in table:

@@ -1,23 +1,59 @@
-"""The command-line drivers bench_expression / bench_binary (the reference's
-src/bench_expression.cpp and src/bench_binary.cpp interfaces): they run the
-tree / contraction on the GPU and check it against the FP64 CUDA-core
-solution of the same inputs; a non-zero exit code means the check failed."""
+"""The command-line drivers bench_expression / bench_binary / bench_tree (the
+reference's src/bench_expression.cpp, src/bench_binary.cpp and
+src/bench_tree.cpp interfaces). Each run is checked twice: by the driver
+itself (against its FP64 CUDA-core solution of the same inputs; a non-zero
+exit code means that check failed) and, independently of the GPU code, by the
+CPU oracle: with EIR_DRIVER_DUMP the driver writes the values its inputs hold
+and its result, and the test recomputes the result with oracle/eir_oracle.c
+along the reference's tree rules (tests/_tree.py) or the parsed tree the
+driver evaluated. Oracle tolerances (relative Frobenius): FP64 1e-12; FP32 and
+BF16 inputs 1e-5 (the oracle stores intermediates as FP32, as the GPU trees
+do); TF32 1e-5 for one contraction and 5e-4 for trees (an intermediate that
+differs by FP32 rounding can round to the neighbouring TF32 value in the next
+contraction)."""
 from __future__ import annotations
 
 import csv as csvmod
+import os
 import re
 import subprocess
 from pathlib import Path
 
+import numpy as np
 import pytest
+
+from einsum_ir_b200 import binary
+from tests import _oracle, _tree
 
 PKG = Path(__file__).resolve().parents[1] / "einsum_ir_b200"
 README = ("iae,bf,dcba,cg,dh->hgfei", "32,8,4,2,16,64,8,8,8", "(1,2),(2,3),(0,1),(0,1)")
 TOL = {"FP32": 1e-5, "FP64": 1e-12, "BF16": 1e-5, "TF32": 1e-2, "CPX_FP32": 1e-5, "CPX_FP64": 1e-12}
+MODEL = {"FP32": "fp32", "FP64": "fp64", "BF16": "fp32", "TF32": "tf32"}
+ORACLE_TOL = {"FP32": 1e-5, "FP64": 1e-12, "BF16": 1e-5, "TF32": 1e-5}
+ORACLE_TOL_TREE = dict(ORACLE_TOL, TF32=5e-4)
 
 
-def _run(args, timeout=300):
-    return subprocess.run([str(a) for a in args], capture_output=True, text=True, timeout=timeout)
+def _run(args, timeout=300, dump=None):
+    env = dict(os.environ)
+    if dump is not None:
+        env["EIR_DRIVER_DUMP"] = str(dump)
+    return subprocess.run([str(a) for a in args], capture_output=True, text=True, timeout=timeout, env=env)
+
+
+def _oracle_expression(dump):
+    """bench_expression's dumped run recomputed with the oracle tree"""
+    man, tensor = _tree.load_dump(dump)
+    n_in = len([k for k in man if k.startswith("in")])
+    ins = [tensor(f"in{t}")[2] for t in range(n_in)]
+    got = tensor("out")[2]
+    expr = man["expr"]
+    if expr[0] == "[":  # standard format -> single characters, dims in sorted-name order
+        tens = [t.strip("[]").split(",") for t in expr.replace("->", "|").replace("],[", "]|[").split("|")]
+        names = sorted({n for t in tens for n in t})
+        ch = {n: chr(ord("a") + i) for i, n in enumerate(names)}
+        expr = ",".join("".join(ch[n] for n in t) for t in tens[:-1]) + "->" + "".join(ch[n] for n in tens[-1])
+    ref = _tree.eval_tree(expr, man["sizes"], man["path"], ins, model=MODEL[man["dtype"]])
+    return _oracle.rel_err(got, ref)
 
 
 def test_drivers_print_usage_without_arguments():
@@ -29,8 +65,8 @@ def test_drivers_print_usage_without_arguments():
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("dtype", ["FP32", "FP64", "BF16", "TF32", "CPX_FP32", "CPX_FP64"])
-def test_bench_expression_readme(cuda, dtype):
-    r = _run([PKG / "bench_expression", *README, dtype, "0", "2"])
+def test_bench_expression_readme(cuda, dtype, tmp_path):
+    r = _run([PKG / "bench_expression", *README, dtype, "0", "2"], dump=tmp_path)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     csv = [l for l in r.stdout.splitlines() if l.startswith("CSV_DATA: einsum_ir_b200,")]
     assert len(csv) == 1
@@ -39,6 +75,9 @@ def test_bench_expression_readme(cuda, dtype):
     assert flops == int(re.search(r"#flops:\s+(\d+)", r.stdout).group(1)) and flops > 1.3e8
     rel = float(re.search(r"relative error:\s+(\S+)", r.stdout).group(1))
     assert rel <= TOL[dtype]
+    if dtype in MODEL:  # complex runs: numpy complex128 in test_gpu_complex.py
+        err = _oracle_expression(tmp_path)
+        assert err <= ORACLE_TOL_TREE[dtype], f"{dtype}: {err:.3e} vs the CPU oracle"
 
 
 @pytest.mark.gpu
@@ -55,10 +94,11 @@ def test_bench_expression_complex_chain(cuda, dtype):
 
 
 @pytest.mark.gpu
-def test_bench_expression_store_lock_and_standard_format(cuda):
+def test_bench_expression_store_lock_and_standard_format(cuda, tmp_path):
     r = _run([PKG / "bench_expression", "[i,a,e],[b,f],[d,c,b,a],[c,g],[d,h]->[h,g,f,e,i]",
-              README[1], README[2], "FP32", "1", "1"])
+              README[1], README[2], "FP32", "1", "1"], dump=tmp_path)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
+    assert _oracle_expression(tmp_path) <= 1e-5
 
 
 @pytest.mark.gpu
@@ -68,12 +108,19 @@ def test_bench_expression_store_lock_and_standard_format(cuda):
     ("abc,acdb->abd", "32,8,4,2", "FP64"),           # the reference driver's usage example
     ("km,nk->nm", "256,256,256", "TF32"),
 ])
-def test_bench_binary(cuda, expr, sizes, dtype):
-    r = _run([PKG / "bench_binary", expr, sizes, dtype])
+def test_bench_binary(cuda, expr, sizes, dtype, tmp_path):
+    r = _run([PKG / "bench_binary", expr, sizes, dtype], dump=tmp_path)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     assert "results are close" in r.stdout
     rel = float(re.search(r"relative error vs FP64 CUDA-core solution: (\S+)", r.stdout).group(1))
     assert rel <= TOL[dtype]
+    # the same run recomputed by the CPU oracle
+    man, tensor = _tree.load_dump(tmp_path)
+    (il, sl, l), (ir, sr, rv), (io, so, got) = tensor("in0"), tensor("in1"), tensor("out")
+    sz = {d: s for ids, sh in ((il, sl), (ir, sr)) for d, s in zip(ids, sh)}
+    dims = binary.contraction_dims(il, ir, io, sz)
+    ref = _tree.contract_step(dims, l, rv, got.size, MODEL[dtype])
+    assert _oracle.rel_err(got, ref) <= ORACLE_TOL[dtype]
 
 
 TREES = [
@@ -97,8 +144,23 @@ TREES = [
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("tree,sizes,dtype", TREES)
-def test_bench_tree(cuda, tree, sizes, dtype):
-    r = _run([PKG / "bench_tree", tree, sizes, dtype])
+def test_bench_tree(cuda, tree, sizes, dtype, tmp_path):
+    r = _run([PKG / "bench_tree", tree, sizes, dtype], dump=tmp_path)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-2000:]
     rel = float(re.search(r"relative error:\s+(\S+)", r.stdout).group(1))
     assert rel <= TOL[dtype]
+    # the parsed tree the driver evaluated, recomputed by the CPU oracle
+    man, tensor = _tree.load_dump(tmp_path)
+    nodes, leaves, sz = [], {}, {}
+    for i in range(len([k for k in man if k.startswith("node")])):
+        f = man[f"node{i}"].split()
+        ids = [] if f[1] == "-" else [int(x) for x in f[1].split(",")]
+        ch = [] if f[3] == "-" else [int(x) for x in f[3].split(",")]
+        nodes.append((ids, ch))
+        if not ch:
+            lids, lsz, leaves[i] = tensor(f"leaf{i}")
+            sz.update(zip(lids, lsz))
+    oids, osz, got = tensor("out")
+    sz.update(zip(oids, osz))
+    ref = _tree.eval_nodes(nodes, sz, leaves, MODEL[dtype])
+    assert _oracle.rel_err(got, ref) <= ORACLE_TOL_TREE[dtype]

@@ -63,6 +63,47 @@ def test_no_alloc_split_k(cuda, monkeypatch):
     assert torch.equal(got, want)  # same kernels, same slices, same summation order
 
 
+def _fp64_plan():
+    # BASELINE config 2's layout in FP64: the K walks disagree, so the DMMA
+    # plan re-lays out the right operand (256 * 64 * 8 doubles = 1 MiB of scratch)
+    il, ir, io, names = binary.parse_binary("akmj,njk->anm")
+    sz = {i: dict(a=2, k=8, m=256, j=64, n=256)[c] for i, c in enumerate(names)}
+    dims = binary.contraction_dims(il, ir, io, sz)
+    plan = cabi.ContractPlan(dims, cabi.FP64, cabi.FP64, cabi.FP64)
+    return plan, ([sz[i] for i in il], [sz[i] for i in ir], [sz[i] for i in io])
+
+
+def test_no_alloc_allocates_nothing_fp64_dmma(cuda, monkeypatch):
+    """On a fresh plan, eir_contract_no_alloc leaves the device's free memory
+    unchanged (eir_contract, by contrast, allocates the plan's workspace on
+    its first call), and matches eir_contract bit for bit (same kernels)."""
+    import torch
+    monkeypatch.setenv("EIR_TC_MIN_OPS", "0")
+    # load the library's device code and run the per-device set-up once
+    warm, (sl, sr, so) = _fp64_plan()
+    l = torch.rand(sl, dtype=torch.float64, device=cuda)
+    r = torch.rand(sr, dtype=torch.float64, device=cuda)
+    o = torch.empty(so, dtype=torch.float64, device=cuda)
+    warm.contract_no_alloc(l, r, o)
+    torch.cuda.synchronize()
+    plan, _ = _fp64_plan()
+    assert plan.family == cabi.FAMILY_DMMA and "prepack=right" in plan.describe(), plan.describe()
+    assert 0 < plan.workspace_bytes <= 8 * 2 ** 20
+    got = torch.full(so, float("nan"), dtype=torch.float64, device=cuda)
+    want = torch.full(so, float("nan"), dtype=torch.float64, device=cuda)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info(cuda)[0]
+    for _ in range(2):
+        plan.contract_no_alloc(l, r, got)
+    torch.cuda.synchronize()
+    cabi.check_device_errors()
+    assert torch.cuda.mem_get_info(cuda)[0] == free0
+    plan.contract(l, r, want)  # allocates the plan's own workspace
+    torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info(cuda)[0] < free0
+    assert torch.equal(got, want)
+
+
 def test_no_alloc_rejects_oversized_scratch(cuda):
     import torch
     # the pre-permuted (smaller) operand is the right one: 512*64*256 BF16 = 16 MiB,
