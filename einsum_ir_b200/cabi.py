@@ -34,7 +34,8 @@ EXPORTS = [
     "eir_last_error_string", "eir_check_device_errors", "eir_launch_count", "eir_version",
     "eir_plan_profile", "eir_plan_profile_read", "eir_contract_no_alloc", "eir_unary_plan_create",
     "eir_contract_peers", "eir_ipc_get_handle", "eir_ipc_open_handle", "eir_ipc_close_handle",
-    "eir_copy_to_peers", "eir_contract_gather",
+    "eir_copy_to_peers", "eir_contract_gather", "eir_output_group_create", "eir_output_group_peers",
+    "eir_output_group_destroy",
     # include/eir_tensor_operation.h
     "eir_top_create", "eir_top_destroy", "eir_top_setup", "eir_top_execute", "eir_top_plan",
     "eir_top_default_optimization_config", "eir_top_optimize",
@@ -63,6 +64,9 @@ class EirError(RuntimeError):
 
 _lib = None
 
+# int (*)(void const *send, void *recv, int64_t bytes, void *user)
+ALLGATHER_FN = ctypes.CFUNCTYPE(ctypes.c_int, c_void_p, c_void_p, c_int64, c_void_p)
+
 
 def lib() -> ctypes.CDLL:
     """Load the shared library once (raises if it is missing)."""
@@ -76,6 +80,10 @@ def lib() -> ctypes.CDLL:
         L.eir_contract_no_alloc.argtypes = [c_void_p] * 6
         L.eir_contract_peers.argtypes = [c_void_p] * 5 + [c_int32, POINTER(c_void_p), c_void_p]
         L.eir_contract_gather.argtypes = [c_void_p] * 5 + [c_int32, POINTER(c_void_p), c_void_p]
+        L.eir_output_group_create.argtypes = [c_int32, c_int32, c_void_p, ALLGATHER_FN, c_void_p,
+                                              POINTER(c_void_p)]
+        L.eir_output_group_peers.argtypes = [c_void_p, c_int64, POINTER(c_void_p)]
+        L.eir_output_group_destroy.argtypes = [c_void_p]
         L.eir_ipc_get_handle.argtypes = [c_void_p, c_void_p, POINTER(c_int64)]
         L.eir_ipc_open_handle.argtypes = [c_void_p, c_int64, POINTER(c_void_p), POINTER(c_void_p)]
         L.eir_ipc_close_handle.argtypes = [c_void_p]
@@ -244,6 +252,44 @@ class ContractPlan(Plan):
 
 
 IPC_HANDLE_BYTES = 64
+
+
+class OutputGroup:
+    """eir_output_group: every rank's full output buffer mapped into this
+    process. `allgather(data: bytes) -> list[bytes]` (one entry per rank, in
+    rank order) is the caller's exchange between the ranks; creation is
+    collective."""
+
+    def __init__(self, rank: int, world: int, out, allgather):
+        def cb(send, recv, nbytes, user):
+            try:
+                parts = allgather(ctypes.string_at(send, nbytes))
+                ctypes.memmove(recv, b"".join(parts), nbytes * world)
+                return 0
+            except Exception:
+                return 1
+        self._cb = ALLGATHER_FN(cb)  # kept alive while the library may call it
+        self.world, self.rank = world, rank
+        h = c_void_p()
+        check(lib().eir_output_group_create(rank, world, _ptr(out), self._cb, None, ctypes.byref(h)))
+        self._h = h
+
+    def peers(self, offset: int) -> list:
+        """addresses in the other ranks' buffers of byte `offset` of this rank's buffer"""
+        arr = (c_void_p * max(1, self.world - 1))()
+        check(lib().eir_output_group_peers(self._h, int(offset), arr))
+        return [int(arr[i] or 0) for i in range(self.world - 1)]
+
+    def close(self) -> None:
+        if getattr(self, "_h", None):
+            lib().eir_output_group_destroy(self._h)
+            self._h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
 
 
 def ipc_get_handle(dev_ptr) -> tuple:

@@ -16,6 +16,7 @@
 #include "EinsumExpression.h"
 #include "EinsumTree.h"
 #include "MemoryManager.h"
+#include "ShardedContraction.h"
 
 using namespace einsum_ir;
 using backend::BinaryContraction;
@@ -275,8 +276,41 @@ static int run_cases() {
   return 0;
 }
 
+// ShardedContraction planning (no GPU needed): BASELINE config 5 over 4
+// ranks, the block of rank 2, the whole job's flops, and the layouts it
+// refuses (sharded dim not outermost, not divisible by the ranks)
+static void test_sharded_contraction() {
+  using einsum_ir::backend::ShardedContraction;
+  std::map<int64_t, int64_t> sizes;
+  for (int64_t d = 0; d < 6; ++d) sizes[d] = 48;
+  sizes[6] = 64;
+  int64_t l[5] = {6, 0, 1, 2, 3}, r[5] = {6, 2, 3, 4, 5}, o[5] = {6, 0, 1, 4, 5};
+  ShardedContraction sc;
+  sc.init(5, 5, 5, &sizes, l, r, o, FP64, 6, 2, 4);
+  CHECK(sc.compile() == SUCCESS);
+  CHECK(sc.block_size() == 16 && sc.block_begin() == 32);
+  CHECK(sc.slab_bytes() == 48 * 48 * 48 * 48 * 8);
+  CHECK(sc.num_ops() == 2 * 64 * 2304LL * 2304LL * 2304LL - 64 * 2304LL * 2304LL);  // ZERO first touch
+  CHECK(sc.contract(nullptr, nullptr, nullptr) == EIR_INVALID_ARGUMENT);  // bind_output first
+  ShardedContraction bad_dim;
+  int64_t o2[5] = {0, 6, 1, 4, 5};
+  bad_dim.init(5, 5, 5, &sizes, l, r, o2, FP64, 6, 0, 4);
+  CHECK(bad_dim.compile() != SUCCESS);
+  ShardedContraction bad_split;
+  bad_split.init(5, 5, 5, &sizes, l, r, o, FP64, 6, 0, 3);
+  CHECK(bad_split.compile() != SUCCESS);
+  // a one-rank output group maps nothing and has no peers
+  double buf[4] = {0, 0, 0, 0};
+  eir_output_group *g = nullptr;
+  CHECK(eir_output_group_create(0, 1, buf, nullptr, nullptr, &g) == EIR_SUCCESS && g != nullptr);
+  CHECK(eir_output_group_peers(g, 16, nullptr) == EIR_SUCCESS);
+  CHECK(eir_output_group_destroy(g) == EIR_SUCCESS);
+  CHECK(eir_output_group_create(1, 1, buf, nullptr, nullptr, &g) == EIR_INVALID_ARGUMENT);
+}
+
 int main(int argc, char **argv) {
   if (argc > 1 && std::string(argv[1]) == "--cases") return run_cases();
+  test_sharded_contraction();
   test_dim_types();
   test_expression_helpers();
   test_swap_inputs();

@@ -8,9 +8,9 @@ with the full output. The gather has three forms:
 
 * ``gather`` (default): ``eir_contract_gather``. The contraction writes rank
   r's block of its own full output, and the copy engines push every finished
-  slab of that block into the other ranks' full outputs (CUDA IPC mappings,
-  handles exchanged over torch.distributed) while the kernel computes the next
-  slabs. One launch covers all of the rank's slabs, so the SMs stay busy to
+  slab of that block into the other ranks' full outputs (mapped by the
+  library's output group, eir_output_group_create, whose CUDA IPC handles
+  travel over torch.distributed) while the kernel computes the next slabs. One launch covers all of the rank's slabs, so the SMs stay busy to
   the end (a launch per slab would leave the last wave of every launch partly
   empty: 324 tiles of 128 x 128 per config-5 slab on 148 SMs); the copies use
   no SM.
@@ -20,7 +20,9 @@ with the full output. The gather has three forms:
   into all ranks' outputs over NVLink.
 
 One process per GPU; torch.distributed is the plumbing (handle exchange,
-barriers, the NCCL fallback), the contraction and the copies are the C-ABI.
+barriers, the NCCL fallback), the contraction, the mappings and the copies
+are the C-ABI. C++ callers use einsum_ir::backend::ShardedContraction
+(csrc/host/ShardedContraction.h; bench_sharded is a driver on top of it).
 ``python -m einsum_ir_b200.sharded`` (under torchrun) runs config 5 and prints
 one JSON line on rank 0.
 """
@@ -74,8 +76,7 @@ class ShardedContraction:
                                       dtype_comp)
         self.world, self.rank = world, rank
         self.num_ops = self.plan.num_ops * world
-        self._peer_ptrs: List[int] = []
-        self._peer_bases: List[int] = []
+        self._group = None
         self._bound = None
 
     def shape(self, ids: Sequence[int], block: bool = False):
@@ -97,55 +98,40 @@ class ShardedContraction:
 
     # ---- peer mappings of every rank's full output
     def bind_output(self, out) -> bool:
-        """Maps every rank's `out` (same shape on all ranks) into this process.
-        Collective over the default process group. False when some rank
-        cannot export or map the buffers (then use run_nccl())."""
+        """Maps every rank's `out` (same shape on all ranks) into this process
+        through the library's output group (eir_output_group_create, CUDA IPC
+        handles exchanged over torch.distributed). Collective over the default
+        process group. False when some rank cannot export or map the buffers
+        (then use run_nccl())."""
         import torch.distributed as dist
         self.unbind()
         if not out.is_contiguous():
             raise ValueError("bind_output: out must be contiguous")
-        if self.world == 1:
-            self._bound = out.data_ptr()
-            return True
+
+        def allgather(data: bytes):
+            parts = [None] * self.world
+            dist.all_gather_object(parts, data)
+            return parts
         try:
-            handle, off = cabi.ipc_get_handle(out)
-            mine = (handle, off, True)
+            self._group = cabi.OutputGroup(self.rank, self.world, out,
+                                           allgather if self.world > 1 else (lambda d: [d]))
         except cabi.EirError:
-            mine = (b"", 0, False)
-        objs = [None] * self.world
-        dist.all_gather_object(objs, mine)
-        ok = all(o[2] for o in objs)
-        ptrs, bases = [], []
-        if ok:
-            try:
-                for r in range(self.world):
-                    if r == self.rank:
-                        continue
-                    ptr, base = cabi.ipc_open_handle(objs[r][0], objs[r][1])
-                    ptrs.append(ptr)
-                    bases.append(base)
-            except cabi.EirError:
-                ok = False
-        flags = [None] * self.world
-        dist.all_gather_object(flags, ok)
-        if not all(flags):
-            for b in bases:
-                cabi.ipc_close_handle(b)
+            self._group = None
             return False
-        self._peer_ptrs, self._peer_bases, self._bound = ptrs, bases, out.data_ptr()
+        self._bound = out.data_ptr()
         return True
 
     def unbind(self) -> None:
         """Closes the peer mappings (every rank, before any rank frees its output)."""
-        for b in self._peer_bases:
-            cabi.ipc_close_handle(b)
-        self._peer_ptrs, self._peer_bases, self._bound = [], [], None
+        if getattr(self, "_group", None) is not None:
+            self._group.close()
+        self._group, self._bound = None, None
 
     def _block_peers(self, out) -> List[int]:
         if self._bound != out.data_ptr():
             raise RuntimeError("bind_output(out) first")
         off = self.layout.owned(self.rank).start * out[0].numel() * out.element_size()
-        return [p + off for p in self._peer_ptrs]
+        return self._group.peers(off) if self.world > 1 else []
 
     # ---- one evaluation (asynchronous on the current stream)
     def run_gather(self, left, right, out, stream=None) -> None:

@@ -190,6 +190,28 @@ int     eir_ipc_get_handle(void const *dev_ptr, void *handle, int64_t *offset);
 int     eir_ipc_open_handle(void const *handle, int64_t offset, void **dev_ptr, void **base);
 int     eir_ipc_close_handle(void *base);
 
+/* --- output group of a sharded contraction (one process per GPU) ---------- */
+/* The caller's exchange between the ranks: every rank passes `bytes` bytes in
+ * `send` and receives all ranks' contributions, in rank order, in `recv`
+ * (world * bytes). Any transport works (MPI_Allgather, NCCL on a device
+ * buffer, sockets, torch.distributed); return 0 on success. */
+typedef int (*eir_allgather_fn)(void const *send, void *recv, int64_t bytes, void *user);
+typedef struct eir_output_group eir_output_group;
+/* Maps the full output buffer `out` of every rank of a node into this
+ * process (CUDA IPC handles exchanged with `allgather`; collective: every
+ * rank calls it with its own buffer of the same size). Fails on every rank
+ * (EIR_CUDA_ERROR) if some rank cannot export or map the buffers. No
+ * counterpart in the reference (it has no multi-GPU path). */
+int     eir_output_group_create(int32_t rank, int32_t world, void *out, eir_allgather_fn allgather,
+                                void *user, eir_output_group **group);
+/* the addresses, in the other ranks' buffers (rank order, this rank left
+ * out: world - 1 entries), that correspond to byte `offset` of this rank's
+ * buffer: the peer list of eir_contract_gather for the block at `offset` */
+int     eir_output_group_peers(eir_output_group const *group, int64_t offset, void **peers);
+/* closes the mappings; every rank destroys its group before any rank frees
+ * its output buffer (e.g. a barrier between the two) */
+int     eir_output_group_destroy(eir_output_group *group);
+
 /* --- unary permute (copy with reordered strides) ------------------------- */
 /* sizes/strides are per dimension, in elements; any order */
 int     eir_permute_plan_create(int32_t num_dims, int64_t const *sizes,

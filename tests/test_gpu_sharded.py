@@ -2,7 +2,11 @@
 the copy-engine gather of finished z-slabs (eir_contract_gather, FP64 and
 TF32), the fused gather (every rank's epilogue stores into all ranks' outputs
 over NVLink) and the NCCL all-gather path, each checked on one z-slab of every
-rank's block against torch. Skipped with fewer than 2 GPUs."""
+rank's block against torch. Skipped with fewer than 2 GPUs. The C++ entry
+point (ShardedContraction, through the bench_sharded driver and its
+file-based handle exchange) runs with one rank on any GPU and with two ranks
+on two GPUs; the driver checks the first slab of every rank's block in its
+gathered output against the FP64 CUDA-core contraction of that slab."""
 from __future__ import annotations
 
 import json
@@ -10,9 +14,12 @@ import os
 import subprocess
 import sys
 
+from pathlib import Path
+
 import pytest
 
 pytestmark = pytest.mark.gpu
+PKG = Path(__file__).resolve().parents[1] / "einsum_ir_b200"
 
 
 def _gpus() -> int:
@@ -35,3 +42,27 @@ def test_sharded_two_ranks(args, tol):
     assert ("NCCL" in res["gather"]) == ("--nccl" in args), res
     if not args or args == ["--fp32", "--tf32"]:
         assert "copy engines" in res["gather"], res
+
+
+def _bench_sharded(tmp_path, world, z, n, dtype):
+    procs = [subprocess.Popen([str(PKG / "bench_sharded"), str(r), str(world), str(tmp_path), str(z), str(n),
+                               dtype], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+             for r in range(world)]
+    outs = []
+    for p in procs:
+        out, err = p.communicate(timeout=300)
+        outs.append((p.returncode, out, err))
+    for rc, out, err in outs:
+        assert rc == 0, out[-2000:] + err[-2000:]
+        assert "CSV_DATA: einsum_ir_b200,bench_sharded," in out
+    return outs
+
+
+@pytest.mark.parametrize("dtype", ["FP64", "FP32"])
+def test_cpp_sharded_contraction_one_rank(cuda, tmp_path, dtype):
+    _bench_sharded(tmp_path, 1, 8, 16, dtype)
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_cpp_sharded_contraction_two_ranks(tmp_path):
+    _bench_sharded(tmp_path, 2, 8, 24, "FP64")
