@@ -17,6 +17,8 @@ than the 126 MB L2), so an ncu capture of them ends in a minute or two:
   bf16_cfg2          BASELINE config 2 (pre-permute + BF16 CTA-pair kernel)
   bf16_mlp_layer     BASELINE config 3, one layer: bi,io->bo, b = 8192, widths 4096, BF16,
                      COPY bias (broadcast over b) first touch, RELU last touch
+  readme_tree        BASELINE config 1: the README expression iae,bf,dcba,cg,dh->hgfei through
+                     eir_expression (FP32; the second and later evaluations replay a CUDA graph)
 """
 from __future__ import annotations
 
@@ -46,6 +48,22 @@ def _contraction(expr, sizes, dt, comp=cabi.COMPUTE_DEFAULT, bias_bcast=None):
     return (lambda: plan.contract(l, r, o, aux)), plan.num_ops, "flop", plan.describe()
 
 
+def _readme_tree():
+    import torch
+    e = cabi.Expression("iae,bf,dcba,cg,dh->hgfei", "32,8,4,2,16,64,8,8,8", "(1,2),(2,3),(0,1),(0,1)",
+                        cabi.FP32)
+    g = torch.Generator(device="cuda").manual_seed(0)
+    ts = [torch.rand(e.tensor_shape(i), generator=g, device="cuda") * 2 - 1 for i in range(e.num_tensors)]
+    st = torch.cuda.Stream()  # graph replay needs a non-default stream
+    torch.cuda.current_stream().wait_stream(st)
+
+    def fn():
+        with torch.cuda.stream(st):
+            e.eval(ts, stream=st.cuda_stream)
+        torch.cuda.current_stream().wait_stream(st)
+    return fn, e.num_ops, "flop", e.describe()
+
+
 def _permute(shape, perm):
     import torch
     x = torch.rand(shape, device="cuda")
@@ -70,6 +88,7 @@ CASES = {
     "bf16_cfg2": lambda: _contraction("akmj,njk->anm", dict(a=16, k=32, m=512, j=64, n=512), cabi.BF16),
     "bf16_mlp_layer": lambda: _contraction("bi,io->bo", dict(b=8192, i=4096, o=4096), cabi.BF16,
                                            bias_bcast="b"),
+    "readme_tree": _readme_tree,
 }
 
 
