@@ -46,6 +46,12 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
+# eir_contract_gather keeps one copy stream per peer waiting on the kernel's
+# slab counters; with CUDA's default 8 hardware work queues those streams
+# share queues with the compute stream and with one another, and a blocked
+# wait then holds back the work queued behind it. Must be set before the CUDA
+# context exists.
+os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
 
 EXPR = "zabcd,zcdef->zabef"
 SIZES = dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48)
@@ -339,6 +345,41 @@ def run_ours(args):
     kern_ms_avg = reduce_max(kern_ms / max(1, kern_n))
     cabi.check_device_errors(sp)
 
+    # ---- N > 1: the step taken apart (after the timed region, same K): the
+    # contraction alone (no gather), the gather alone (this rank's finished block
+    # copied to every peer, one copy stream per peer), and the overlapped step above
+    breakdown = None
+    if world > 1:
+        def timed(fn):
+            barrier()
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record(stream)
+            for _ in range(args.steps):
+                fn()
+            b.record(stream)
+            barrier()
+            return reduce_max(a.elapsed_time(b) / args.steps)
+
+        copy_streams = [torch.cuda.Stream(dev) for _ in peers]
+        blk_bytes = out_blk.numel() * 8
+
+        def gather_only():
+            fork = torch.cuda.Event()
+            fork.record(stream)
+            for cs, p in zip(copy_streams, peers):
+                cs.wait_event(fork)
+                cabi.copy_to_peers(out_blk, [p], blk_bytes, stream=cs.cuda_stream)
+                join = torch.cuda.Event()
+                join.record(cs)
+                stream.wait_event(join)
+
+        breakdown = {"compute_only_ms": timed(lambda: plan.contract(l, r, out_blk, stream=sp)),
+                     "gather_only_ms": timed(gather_only),
+                     "overlapped_ms": step_ms_max / args.steps,
+                     "gather_bytes_per_rank": blk_bytes * len(peers),
+                     "note": "max over ranks; gather_only = cudaMemcpyAsync of the rank's block to each "
+                             "peer on its own stream, no contraction"}
+
     # ---- correctness spot check: one z-slab of every rank's block vs torch (fp64)
     errs = []
     for rr in range(world):
@@ -419,7 +460,9 @@ def run_ours(args):
                            "rank's full output, inside the step" if world > 1 else "whole job"),
                        "l2": "no flush: each operand (2.72 GB, or its z block) is larger than L2",
                        "plan": plan.describe(), "rel_err_vs_torch_fp64": rel,
+                       "cuda_device_max_connections": os.environ.get("CUDA_DEVICE_MAX_CONNECTIONS"),
                        "gathered_output_finite": gathered_finite},
+            "step_breakdown": breakdown,
             "e2e": {"value": e2e_value, "unit": "TFLOP/s",
                     "h2d_bytes_per_step": (l.numel() + r.numel()) * 8,
                     "d2h_bytes_per_step": out_blk.numel() * 8,

@@ -19,6 +19,7 @@
 #include <unistd.h>
 #include <chrono>
 #include <cstdio>
+#include <cstdlib>
 #include <map>
 #include <string>
 #include <thread>
@@ -92,6 +93,10 @@ int main(int argc, char *argv[]) {
                  "  * z, size, dtype: zabcd,zcdef->zabef sizes (default 64 48) and FP64 (default) or FP32\n");
     return EXIT_FAILURE;
   }
+  // one hardware queue per stream (before the CUDA context exists): the copy
+  // streams of eir_contract_gather wait on the kernel's slab counters, and a
+  // blocked wait in a shared queue holds back the work behind it
+  setenv("CUDA_DEVICE_MAX_CONNECTIONS", "32", 0);
   FileExchange x;
   x.rank = std::atoi(argv[1]);
   x.world = std::atoi(argv[2]);

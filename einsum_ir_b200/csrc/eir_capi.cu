@@ -186,6 +186,60 @@ int64_t env_int(char const *name, int64_t dflt) {
   return std::atoll(v);
 }
 
+// ceil(2^64 / d) for 2 <= d < 2^32: the multiplier of div_magic (kernels_simt.cu)
+uint64_t magic_of(int64_t d) { return d >= 2 ? UINT64_MAX / (uint64_t)d + 1 : 0; }
+
+// The direct CUDA-core kernel's parameters (eir::DirectParams) from the
+// plan's dims and SIMT groups. The CUDA-core path takes it for tiny problems:
+// fewer than 2^22 outputs (the 32-bit index decomposition) and a short K
+// walk per output (K <= 64, or outputs x K <= 2^16). EIR_SIMT_DIRECT=0 keeps
+// the tiled kernel.
+void build_direct(eir_plan *p) {
+  eir::DirectParams &d = p->direct;
+  d = eir::DirectParams{};
+  std::vector<LDim> od;
+  for (auto const &x : p->dims)
+    if (x.type != EIR_DIM_K) od.push_back(x);
+  if ((int)od.size() > eir::kMaxDirectDims) return;
+  std::stable_sort(od.begin(), od.end(),
+                   [](LDim const &a, LDim const &b) { return std::llabs(a.so) < std::llabs(b.so); });
+  int64_t total = 1;
+  for (auto const &x : od) total *= x.size;
+  const eir::GroupDims &k = p->simt.k;
+  const int64_t k_total = k.total;
+  const bool small = total < (int64_t(1) << 22) &&
+                     (k_total <= 64 || (double)total * (double)k_total <= (double)(1 << 16));
+  if (!small || env_int("EIR_SIMT_DIRECT", 1) == 0) return;
+  d.nd = (int32_t)od.size();
+  for (int i = 0; i < d.nd; ++i) {
+    d.size[i] = (uint32_t)od[i].size;
+    d.magic[i] = magic_of(od[i].size);
+    d.sl[i] = od[i].sl;
+    d.sr[i] = od[i].sr;
+    d.so[i] = od[i].so;
+    d.sa[i] = od[i].sa;
+  }
+  d.nk = k.n;
+  for (int i = 0; i < k.n; ++i) {
+    d.ksize[i] = (uint32_t)k.size[i];
+    d.kmagic[i] = magic_of(k.size[i]);
+    d.ksl[i] = k.sl[i];
+    d.ksr[i] = k.sr[i];
+  }
+  d.total = total;
+  if (k_total == 0) {
+    d.k_inner = 0;
+    d.k_outer = 0;
+  } else {
+    d.k_inner = k.n > 0 ? k.size[0] : 1;
+    d.k_outer = k_total / d.k_inner;
+  }
+  d.first_touch = p->simt.first_touch;
+  d.last_touch = p->simt.last_touch;
+  d.round_tf32 = p->simt.round_tf32;
+  p->simt_direct = true;
+}
+
 // Permute planning shared by eir_permute_plan_create and operand pre-packing.
 int plan_permute(int nd, int64_t const *sizes, int64_t const *sin, int64_t const *sout, int esize,
                  eir::PermuteParams *pp, std::string *text) {
@@ -766,9 +820,16 @@ struct ProfScope {
 int run_simt(eir_plan *p, void const *l, void const *r, void const *aux, void *out,
              eir::PeerOutputs const *peers, cudaStream_t st) {
   ProfScope prof(p, st);
-  eir::SimtParams sp = p->simt;
-  if (peers != nullptr) sp.peers = *peers;
-  cudaError_t e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, sp, l, r, aux, out, st);
+  cudaError_t e;
+  if (p->simt_direct) {
+    eir::DirectParams dp = p->direct;
+    if (peers != nullptr) dp.peers = *peers;
+    e = eir::launch_simt_direct(p->dt_l, p->dt_r, p->dt_o, dp, l, r, aux, out, st);
+  } else {
+    eir::SimtParams sp = p->simt;
+    if (peers != nullptr) sp.peers = *peers;
+    e = eir::launch_simt_contract(p->dt_l, p->dt_r, p->dt_o, sp, l, r, aux, out, st);
+  }
   if (e != cudaSuccess) return cuda_fail(e, "simt contraction launch");
   g_launches.fetch_add(1, std::memory_order_relaxed);
   return EIR_SUCCESS;
@@ -1022,6 +1083,7 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
   p->simt.b_kfast = min_abs_stride(p->dims, EIR_DIM_K, false) < min_abs_stride(p->dims, EIR_DIM_N, false);
   p->simt.m_tiles = ceil_div(p->simt.m.total, 64);
   p->simt.n_tiles = ceil_div(p->simt.n.total, 64);
+  build_direct(p);
 
   std::string why = "forced";
   if (!p->empty && !(desc->flags & EIR_FLAG_FORCE_SIMT) && try_tc(p, &why)) {
@@ -1036,7 +1098,8 @@ int eir_contract_plan_create(eir_contract_desc const *desc, eir_plan **plan_out)
     dims_txt += std::to_string(x.size) + " ";
   }
   const bool tensor_cores = p->family == EIR_FAMILY_TC || p->family == EIR_FAMILY_DMMA;
-  p->text = (tensor_cores ? why : "simt (" + why + ")") + " | dims: " + dims_txt;
+  p->text = (tensor_cores ? why : "simt (" + why + (p->simt_direct ? "; one output per thread" : "") + ")") +
+            " | dims: " + dims_txt;
   if (p->swapped) p->text += "| operands swapped (output contiguous along the right operand) ";
   if (p->out_dense)
     p->text += "| gather: " + std::to_string(p->slab_count) + " slab(s)" +

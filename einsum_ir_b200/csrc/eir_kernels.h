@@ -10,6 +10,10 @@ namespace eir {
 cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const &p, void const *l,
                                  void const *r, void const *aux, void *out, cudaStream_t st);
 
+// the direct (one output per thread) CUDA-core contraction of tiny problems
+cudaError_t launch_simt_direct(int dt_l, int dt_r, int dt_o, DirectParams const &p, void const *l,
+                               void const *r, void const *aux, void *out, cudaStream_t st);
+
 // split-K reduction of a split tcgen05 plan (TcParams::split_k): p is the
 // plan's real parameter block (output strides and touches), ws the workspace
 cudaError_t launch_splitk_reduce(TcParams const &p, float const *ws, float const *aux, float *out,

@@ -45,6 +45,38 @@ struct SimtParams {
   PeerOutputs peers;
 };
 
+// The direct CUDA-core contraction (one output element per thread) for tiny
+// problems: the C, M and N dims form one output index (fastest output stride
+// first), decomposed with 32-bit quotients q = mulhi64(x, magic), magic =
+// ceil(2^64 / size), which is exact for x < 2^32 (Lemire, Kaser, Kurz,
+// "Faster Remainder by Direct Computation", 2019); the planner only takes
+// this kernel for fewer than 2^22 outputs. K runs as an inner loop over K
+// dim 0 (fastest left stride) inside an outer loop over the other K dims.
+constexpr int kMaxDirectDims = 3 * kMaxGroupDims;
+
+struct DirectParams {
+  int32_t nd = 0;            // output-index dims
+  int32_t nk = 0;            // K dims
+  int32_t first_touch = 0;   // EIR_KTYPE_*
+  int32_t last_touch = 0;
+  int32_t round_tf32 = 0;
+  int32_t pad_ = 0;
+  int64_t total = 0;         // output elements (< 2^22)
+  int64_t k_inner = 1;       // size of K dim 0 (1 without K dims)
+  int64_t k_outer = 1;       // product of the other K dims (0 when a K dim is empty)
+  uint32_t size[kMaxDirectDims] = {};
+  uint64_t magic[kMaxDirectDims] = {};   // ceil(2^64 / size); unused for size 1
+  int64_t sl[kMaxDirectDims] = {};
+  int64_t sr[kMaxDirectDims] = {};
+  int64_t so[kMaxDirectDims] = {};
+  int64_t sa[kMaxDirectDims] = {};
+  uint32_t ksize[kMaxGroupDims] = {};
+  uint64_t kmagic[kMaxGroupDims] = {};
+  int64_t ksl[kMaxGroupDims] = {};
+  int64_t ksr[kMaxGroupDims] = {};
+  PeerOutputs peers;
+};
+
 // Permute: dims sorted so that dim 0 is the output's fastest dim.
 struct PermuteParams {
   int32_t nd = 0;

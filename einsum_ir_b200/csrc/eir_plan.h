@@ -81,6 +81,8 @@ struct eir_plan {
   bool swapped = false;          // left and right change roles (dims and dt_l / dt_r are the swapped ones)
   std::vector<eir::LDim> dims;   // after size-1 removal and fusion
   eir::SimtParams simt;
+  eir::DirectParams direct;      // the CUDA-core path of tiny problems (one output per thread)
+  bool simt_direct = false;      // the CUDA-core path takes `direct`, not the tiled `simt`
   bool tc = false;
   // complex contraction: the right operand is expanded into real blocks
   // (cpx_expand, into the workspace) and `cpx_inner` contracts the real problem

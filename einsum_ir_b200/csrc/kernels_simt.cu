@@ -234,6 +234,98 @@ cudaError_t launch_simt_contract(int dt_l, int dt_r, int dt_o, SimtParams const 
   return cudaErrorInvalidValue;
 }
 
+// ------------------------------------------------------------ direct kernel
+// One output element per thread, for contractions too small to fill the 64 x
+// 64 tiles above (trees of small tensors): the tiled kernel's fixed cost (a
+// long, cold instruction stream per CTA) then dominates. Same semantics and
+// chunked accumulation as the tiled kernel.
+__device__ __forceinline__ uint32_t div_magic(uint32_t x, uint32_t size, uint64_t magic) {
+  return size == 1u ? x : (uint32_t)__umul64hi((uint64_t)x, magic);
+}
+
+template <typename TL, typename TR, typename TO, typename TA>
+__global__ void __launch_bounds__(256)
+    simt_direct_kernel(const DirectParams p, const TL *__restrict__ L, const TR *__restrict__ R,
+                       const TO *__restrict__ AUX, TO *__restrict__ OUT) {
+  pdl_launch_dependents();
+  pdl_wait();
+  const int64_t gid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (gid >= p.total) return;
+  uint32_t x = (uint32_t)gid;
+  int64_t ol = 0, orr = 0, oo = 0, oa = 0;
+#pragma unroll 1
+  for (int d = 0; d < p.nd; ++d) {
+    const uint32_t q = div_magic(x, p.size[d], p.magic[d]);
+    const int64_t i = (int64_t)(x - q * p.size[d]);
+    x = q;
+    ol += i * p.sl[d];
+    orr += i * p.sr[d];
+    oo += i * p.so[d];
+    oa += i * p.sa[d];
+  }
+  TA acc = TA(0), tot = TA(0);
+  int chunk = 0;
+  const int64_t s_l = p.ksl[0], s_r = p.ksr[0];
+#pragma unroll 1
+  for (int64_t j = 0; j < p.k_outer; ++j) {
+    int64_t bl = ol, br = orr;
+    uint32_t y = (uint32_t)j;
+#pragma unroll 1
+    for (int d = 1; d < p.nk; ++d) {
+      const uint32_t q = div_magic(y, p.ksize[d], p.kmagic[d]);
+      const int64_t i = (int64_t)(y - q * p.ksize[d]);
+      y = q;
+      bl += i * p.ksl[d];
+      br += i * p.ksr[d];
+    }
+#pragma unroll 4
+    for (int64_t i = 0; i < p.k_inner; ++i) {
+      acc += load_acc<TA>(L[bl + i * s_l], p.round_tf32) * load_acc<TA>(R[br + i * s_r], p.round_tf32);
+      if (++chunk == kSimtChunkK) {
+        tot += acc;
+        acc = TA(0);
+        chunk = 0;
+      }
+    }
+  }
+  TA v = tot + acc;
+  if (p.first_touch == 3 /*COPY*/) v += static_cast<TA>(AUX[oa]);
+  else if (p.first_touch == 2 /*ADD*/) v += static_cast<TA>(OUT[oo]) + static_cast<TA>(AUX[oa]);
+  else if (p.first_touch != 0 /*ZERO*/) v += static_cast<TA>(OUT[oo]);
+  if (p.last_touch == 1 /*RELU*/) v = v > TA(0) ? v : TA(0);
+  else if (p.last_touch == 2 /*ADD*/) v += static_cast<TA>(AUX[oa]);
+  OUT[oo] = static_cast<TO>(v);
+  for (int q = 0; q < p.peers.n; ++q) static_cast<TO *>(p.peers.ptr[q])[oo] = static_cast<TO>(v);
+}
+
+template <typename TL, typename TR, typename TO, typename TA>
+static cudaError_t launch_direct_t(DirectParams const &p, void const *l, void const *r, void const *aux,
+                                   void *out, cudaStream_t st) {
+  if (p.total <= 0) return cudaSuccess;
+  if (p.total >= (int64_t(1) << 32)) return cudaErrorInvalidConfiguration;
+  const int64_t blocks = (p.total + 255) / 256;
+  return launch_kernel(simt_direct_kernel<TL, TR, TO, TA>, dim3((unsigned)blocks), dim3(256), 0, st, p,
+                       static_cast<TL const *>(l), static_cast<TR const *>(r), static_cast<TO const *>(aux),
+                       static_cast<TO *>(out));
+}
+
+cudaError_t launch_simt_direct(int dt_l, int dt_r, int dt_o, DirectParams const &p, void const *l,
+                               void const *r, void const *aux, void *out, cudaStream_t st) {
+  if (dt_o == 1) {
+    if (dt_l == 1 && dt_r == 1) return launch_direct_t<double, double, double, double>(p, l, r, aux, out, st);
+    return cudaErrorInvalidValue;
+  }
+  if (dt_o != 0) return cudaErrorInvalidValue;
+  if (dt_l == 0 && dt_r == 0) return launch_direct_t<float, float, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 2 && dt_r == 2)
+    return launch_direct_t<__nv_bfloat16, __nv_bfloat16, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 2 && dt_r == 0)
+    return launch_direct_t<__nv_bfloat16, float, float, float>(p, l, r, aux, out, st);
+  if (dt_l == 0 && dt_r == 2)
+    return launch_direct_t<float, __nv_bfloat16, float, float>(p, l, r, aux, out, st);
+  return cudaErrorInvalidValue;
+}
+
 // ------------------------------------------------------------------ permute
 // an element as copied by a permute: FP32 words rounded to the nearest TF32
 // value when the permute feeds a TF32 contraction (PermuteParams::round_tf32)

@@ -13,7 +13,11 @@ with the full output. The gather has three forms:
   travel over torch.distributed) while the kernel computes the next slabs. One launch covers all of the rank's slabs, so the SMs stay busy to
   the end (a launch per slab would leave the last wave of every launch partly
   empty: 324 tiles of 128 x 128 per config-5 slab on 148 SMs); the copies use
-  no SM.
+  no SM. The process should run with CUDA_DEVICE_MAX_CONNECTIONS >= 16, set
+  before its CUDA context exists (``_main`` and bench.py set 32): with CUDA's
+  default 8 hardware queues the waiting copy streams share queues with the
+  compute stream and with one another, and at 8 GPUs the step then takes
+  9.2 ms instead of 6.8 ms.
 * ``nccl``: the contraction, then an in-place NCCL ``all_gather_into_tensor``
   of the rank blocks (for processes that cannot map each other's memory).
 * ``fused``: ``eir_contract_peers``, the epilogue stores every output element
@@ -165,6 +169,10 @@ class ShardedContraction:
 
 
 def _main() -> int:
+    # the copy streams of eir_contract_gather wait on the kernel's slab
+    # counters: give every stream its own hardware queue (before the CUDA
+    # context exists) so a blocked wait holds back no other stream's work
+    os.environ.setdefault("CUDA_DEVICE_MAX_CONNECTIONS", "32")
     import torch
     import torch.distributed as dist
     from datetime import timedelta

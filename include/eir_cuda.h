@@ -168,9 +168,14 @@ int     eir_contract_peers(eir_plan *plan, void const *left, void const *right,
  * output and every peer copy are complete; a reader on another GPU first
  * synchronises with this rank (e.g. a stream synchronisation, then a
  * cross-process barrier). Like every workspace-owning plan, one plan must
- * not run on two streams at once. Not for complex plans. No counterpart in
- * the reference (it has no multi-GPU path; BASELINE config 5 shards its
- * batch dim z across GPUs and all-gathers the output). */
+ * not run on two streams at once. Not for complex plans. The copy streams
+ * wait on the kernel's slab counters: run the process with
+ * CUDA_DEVICE_MAX_CONNECTIONS >= 16 (set before its CUDA context exists), or
+ * with CUDA's default of 8 hardware queues the waiting streams share queues
+ * with the compute stream and with one another and hold back the work
+ * behind them. No counterpart in the reference (it has no multi-GPU path;
+ * BASELINE config 5 shards its batch dim z across GPUs and all-gathers the
+ * output). */
 int     eir_contract_gather(eir_plan *plan, void const *left, void const *right,
                             void const *out_aux, void *out, int32_t num_peers,
                             void *const *peer_outs, void *stream);

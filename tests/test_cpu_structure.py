@@ -176,6 +176,8 @@ PLAN_CASES = [
     ("zcdef,zabcd->zabef", dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48), cabi.FP64, 0,
      ["tc kind=fp64-dmma", "A=MN B=K"]),
     ("acfh,acegi->hgfei", dict(a=32, c=4, e=16, f=64, g=8, h=8, i=8), cabi.FP32, 0, ["simt"]),
+    # the README tree's first step: tiny, one output element per thread
+    ("dcba,bf->facd", dict(a=32, b=8, c=4, d=2, f=64), cabi.FP32, 0, ["simt (", "one output per thread"]),
     # output contiguous along the right operand: the planner swaps the roles
     ("bi,io->bo", dict(b=8192, i=4096, o=4096), cabi.BF16, 0, ["tc kind=bf16", "A=MN B=K", "operands swapped"]),
     ("zabcd,zcdef->zabef", dict(z=64, a=48, b=48, c=48, d=48, e=48, f=48), cabi.FP64, 0,

@@ -44,14 +44,17 @@ def _np_in(t):
 
 def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
              last=cabi.KTYPE_UNDEFINED, aux_outer=None, flags=0, seed=0, expect_family=None,
-             tf32_general=False, tc_min_ops="0", pair=None, bn=None, ksub=None, tol=None):
+             tf32_general=False, tc_min_ops="0", pair=None, bn=None, ksub=None, tol=None, direct=None):
     """pair / bn / ksub force the tensor-core tile shape (CTA pair or one CTA,
-    BN, K blocks per stage); None leaves the planner's choice. tol overrides
-    the dtype's tolerance."""
+    BN, K blocks per stage); None leaves the planner's choice. direct: True
+    expects the one-output-per-thread CUDA-core kernel, False keeps the tiled
+    one. tol overrides the dtype's tolerance."""
     import torch
     os.environ["EIR_TC_MIN_OPS"] = tc_min_ops
     os.environ["EIR_TC_MIN_UTIL"] = "0"
-    for var, val in (("EIR_TC_PAIR", pair), ("EIR_TC_BN", bn), ("EIR_TC_KSUB", ksub)):
+    direct_env = None if direct is None else ("1" if direct else "0")
+    for var, val in (("EIR_TC_PAIR", pair), ("EIR_TC_BN", bn), ("EIR_TC_KSUB", ksub),
+                     ("EIR_SIMT_DIRECT", direct_env)):
         if val is None:
             os.environ.pop(var, None)
         else:
@@ -69,6 +72,8 @@ def run_case(cuda, expr, sizes, dtype="fp32", comp=None, first=cabi.KTYPE_ZERO,
     plan = cabi.ContractPlan(dims, dt, dt, dto, comp, first, cabi.KTYPE_MADD, last, flags)
     if expect_family is not None:
         assert plan.family == expect_family, plan.describe()
+    if direct is not None:
+        assert ("one output per thread" in plan.describe()) == direct, plan.describe()
 
     shape = lambda ids: [sz[i] for i in ids]
     l, r = _make_inputs(torch, shape(il), shape(ir), dtype, seed,
@@ -307,9 +312,50 @@ SIMT_CASES = [
 ]
 
 
+# the cases the planner gives the one-output-per-thread kernel (fewer than
+# 2^22 outputs, K <= 64 or outputs x K <= 2^16); the last SIMT case (K = 96,
+# 32768 outputs) stays on the tiled kernel
+SIMT_DIRECT_CASES = SIMT_CASES[:-1]
+
+
 @pytest.mark.parametrize("expr,sizes,dtype", SIMT_CASES)
 def test_simt_parity(cuda, expr, sizes, dtype):
-    run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT)
+    # the tiled 64 x 64 kernel (the direct kernel switched off)
+    run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT, direct=False)
+
+
+@pytest.mark.parametrize("expr,sizes,dtype", SIMT_DIRECT_CASES)
+def test_simt_direct_parity(cuda, expr, sizes, dtype):
+    run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT, direct=True)
+
+
+def test_simt_default_choice(cuda):
+    # the planner's own choice (no override): tiled for the K = 96 case
+    run_case(cuda, *SIMT_CASES[-1], flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT)
+
+
+@pytest.mark.parametrize("expr,sizes,dtype", [
+    ("mk,nk->nm", dict(m=2, n=2, k=16384), "fp32"),      # 64 accumulation chunks of 256
+    ("mk,nk->nm", dict(m=2, n=2, k=16384), "fp64"),
+    ("abkq,qk->ab", dict(a=3, b=4, k=1000, q=5), "fp32"),  # two K dims, the outer one walked
+    ("zab,zbc->zac", dict(z=5, a=7, b=9, c=6), "bf16"),
+])
+def test_simt_direct_long_k(cuda, expr, sizes, dtype):
+    run_case(cuda, expr, sizes, dtype, flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT, direct=True)
+
+
+@pytest.mark.parametrize("first,last", [(cabi.KTYPE_UNDEFINED, cabi.KTYPE_UNDEFINED),
+                                        (cabi.KTYPE_ADD, cabi.KTYPE_UNDEFINED),
+                                        (cabi.KTYPE_ZERO, cabi.KTYPE_ADD),
+                                        (cabi.KTYPE_COPY, cabi.KTYPE_RELU)])
+def test_simt_direct_touches(cuda, first, last):
+    run_case(cuda, "mk,nk->nm", dict(m=33, n=17, k=9), "fp32", first=first, last=last, aux_outer="n",
+             flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT, direct=True)
+
+
+def test_simt_direct_tf32_general_inputs(cuda):
+    run_case(cuda, "zab,zbc->zac", dict(z=5, a=7, b=9, c=6), "tf32", tf32_general=True,
+             flags=cabi.FLAG_FORCE_SIMT, expect_family=SIMT, direct=True)
 
 
 def test_simt_long_k(cuda):
