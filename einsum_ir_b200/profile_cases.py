@@ -19,6 +19,9 @@ than the 126 MB L2), so an ncu capture of them ends in a minute or two:
                      COPY bias (broadcast over b) first touch, RELU last touch
   readme_tree        BASELINE config 1: the README expression iae,bf,dcba,cg,dh->hgfei through
                      eir_expression (FP32; the second and later evaluations replay a CUDA graph)
+  tucker             BASELINE config 4: abc,ia,jb,kc->ijk, core 128^3, factors 1024 x 128, path
+                     (0,1),(0,2),(0,1), FP32 through eir_expression (4.29 GB output: a few GB on
+                     the device, too large for an ncu capture; time it with --time)
 """
 from __future__ import annotations
 
@@ -49,9 +52,16 @@ def _contraction(expr, sizes, dt, comp=cabi.COMPUTE_DEFAULT, bias_bcast=None):
 
 
 def _readme_tree():
+    return _expression("iae,bf,dcba,cg,dh->hgfei", "32,8,4,2,16,64,8,8,8", "(1,2),(2,3),(0,1),(0,1)")
+
+
+def _tucker():
+    return _expression("abc,ia,jb,kc->ijk", "128,128,128,1024,1024,1024", "(0,1),(0,2),(0,1)")
+
+
+def _expression(expr, sizes, path):
     import torch
-    e = cabi.Expression("iae,bf,dcba,cg,dh->hgfei", "32,8,4,2,16,64,8,8,8", "(1,2),(2,3),(0,1),(0,1)",
-                        cabi.FP32)
+    e = cabi.Expression(expr, sizes, path, cabi.FP32)
     g = torch.Generator(device="cuda").manual_seed(0)
     ts = [torch.rand(e.tensor_shape(i), generator=g, device="cuda") * 2 - 1 for i in range(e.num_tensors)]
     st = torch.cuda.Stream()  # graph replay needs a non-default stream
@@ -89,6 +99,7 @@ CASES = {
     "bf16_mlp_layer": lambda: _contraction("bi,io->bo", dict(b=8192, i=4096, o=4096), cabi.BF16,
                                            bias_bcast="b"),
     "readme_tree": _readme_tree,
+    "tucker": _tucker,
 }
 
 
