@@ -392,8 +392,11 @@ def run_ours(args):
 
     # ---- end to end with host buffers: pinned H2D of this rank's input blocks,
     # contraction (+ gather), D2H of this rank's block of the result, pipelined
-    # over groups of z-slabs on three streams
-    n_groups = min(8, zb)
+    # over groups of z-slabs on three streams. The step is bound by PCIe (the
+    # H2D of 2 x the output's bytes); the first group's H2D and the last
+    # group's contraction and D2H are not overlapped, so groups are small (two
+    # slabs, 85 MB of output, at N = 1)
+    n_groups = min(32, zb)
     gz = zb // n_groups
     from einsum_ir_b200 import binary
     g_sizes = dict(SIZES, z=gz)
