@@ -198,6 +198,28 @@ def test_lowering_decisions(expr, sizes, dt, comp, frags, monkeypatch):
         assert f in d, d
 
 
+@pytest.mark.parametrize("expr,sizes,direct", [
+    ("mk,nk->nm", dict(m=32, n=32, k=64), True),        # K <= 64
+    ("mk,nk->nm", dict(m=32, n=32, k=65), False),       # K > 64 and outputs x K > 2^16
+    ("mk,nk->nm", dict(m=2, n=2, k=16384), True),       # outputs x K = 2^16
+    ("mk,nk->nm", dict(m=2, n=2, k=16385), False),
+    ("mn,n->mn", dict(m=2048, n=2047), True),           # no K dim, 2^22 - 2048 outputs
+    ("mn,n->mn", dict(m=2048, n=2048), False),          # 2^22 outputs
+])
+def test_simt_direct_eligibility(expr, sizes, direct, monkeypatch):
+    # the one-output-per-thread CUDA-core kernel takes fewer than 2^22 outputs
+    # with K <= 64 or outputs x K <= 2^16; EIR_SIMT_DIRECT=0 keeps the tiled one
+    il, ir, io, names = binary.parse_binary(expr)
+    sz = {i: sizes[c] for i, c in enumerate(names)}
+    dims = binary.contraction_dims(il, ir, io, sz)
+    monkeypatch.delenv("EIR_SIMT_DIRECT", raising=False)
+    plan = cabi.ContractPlan(dims, cabi.FP32, cabi.FP32, cabi.FP32, flags=cabi.FLAG_FORCE_SIMT)
+    assert ("one output per thread" in plan.describe()) == direct, plan.describe()
+    monkeypatch.setenv("EIR_SIMT_DIRECT", "0")
+    plan = cabi.ContractPlan(dims, cabi.FP32, cabi.FP32, cabi.FP32, flags=cabi.FLAG_FORCE_SIMT)
+    assert "one output per thread" not in plan.describe(), plan.describe()
+
+
 def test_error_codes():
     dims = [(cabi.DIM_M, 4, 1, 0, 1, 0), (cabi.DIM_N, 4, 0, 1, 4, 0), (cabi.DIM_K, 4, 4, 4, 0, 0)]
     with pytest.raises(cabi.EirError) as e:
