@@ -174,3 +174,42 @@ def test_golden_fixtures_equal_reference():
     t = _ref_binary("bci,jb->cij", t, d["in2"])
     t = _ref_binary("cij,kc->ijk", t, d["in3"])
     assert _oracle.rel_err(t, d["out"]) <= 1e-12
+
+
+def test_readme_tree_fixture_equals_reference():
+    """the README expression iae,bf,dcba,cg,dh->hgfei (path (1,2),(2,3),(0,1),(0,1))
+    evaluated binary step by step through the reference's scalar backend, with
+    the intermediates its tree rules give (dims in ascending id order:
+    EinsumExpression.cpp:25-99), equals the committed FP64 golden output"""
+    d = np.load(GOLDEN / "readme_tree_fp64.npz", allow_pickle=False)
+    acdf = _ref_binary("bf,dcba->acdf", d["in1"], d["in2"])
+    acfh = _ref_binary("dh,acdf->acfh", d["in4"], acdf)
+    acegi = _ref_binary("iae,cg->acegi", d["in0"], d["in3"])
+    out = _ref_binary("acfh,acegi->hgfei", acfh, acegi)
+    assert _oracle.rel_err(out, d["out"]) <= 1e-12
+
+
+def test_mlp_layer_fixture_equals_reference():
+    """one bench_mlp hidden layer, relu(x w + bias), through the reference's
+    scalar backend: COPY first touch of the bias broadcast over b (outer size
+    1, so stride 0), MADD, RELU last touch (ContractionBackendScalar.cpp:70-115),
+    on the fixture's inputs in FP64, equals the committed golden output"""
+    d = np.load(GOLDEN / "cfg3_mlp_layer.npz", allow_pickle=False)
+    x, w, bias = (d[k].astype(np.float64) for k in ("x", "w", "bias"))
+    il, ir, io, names = binary.parse_binary("bi,io->bo")
+    sz = {i: n for i, n in zip(range(3), (x.shape[0], x.shape[1], w.shape[1]))}  # b, i, o
+    aux_outer = {i: (1 if names[i] == "b" else sz[i]) for i in sz}
+    out = np.zeros([sz[i] for i in io])
+    c = _refscalar.Contraction(il, ir, io, sz, dtype=cabi.FP64, first=cabi.KTYPE_COPY, last=cabi.KTYPE_RELU,
+                               aux_outer=aux_outer, threads=1)
+    c.contract(np.ascontiguousarray(x), np.ascontiguousarray(w), out, bias.reshape(1, -1).copy())
+    assert _oracle.rel_err(out, d["out"]) <= 1e-12
+
+
+@pytest.mark.parametrize("dtype", [cabi.FP32, cabi.FP64])
+def test_long_k_equals_reference(dtype):
+    """K = 6144 over two K dims: the reference's scalar backend sums in the
+    data type (an FP32 running sum for FP32), the oracle in FP64 / long double;
+    they agree to the FP32 tolerance"""
+    got, ref, _, _ = _both("mkq,nqk->nm", dict(m=5, n=6, k=1024, q=6), dtype, seed=9)
+    assert _oracle.rel_err(got, ref) <= TOL[dtype]
