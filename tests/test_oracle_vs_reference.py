@@ -213,3 +213,14 @@ def test_long_k_equals_reference(dtype):
     they agree to the FP32 tolerance"""
     got, ref, _, _ = _both("mkq,nqk->nm", dict(m=5, n=6, k=1024, q=6), dtype, seed=9)
     assert _oracle.rel_err(got, ref) <= TOL[dtype]
+
+
+def test_bf16_fixture_equals_reference_fp64():
+    """config 2 (akmj,njk->anm) has BF16 inputs, which the reference cannot
+    read; every BF16 value is exact in FP64, so the reference's FP64 scalar
+    backend on the fixture's inputs gives the exact products the golden
+    output holds"""
+    d = np.load(GOLDEN / "cfg2_binary_bf16.npz", allow_pickle=False)
+    as_f64 = lambda u: (u.astype(np.uint32) << 16).view(np.float32).astype(np.float64)
+    out = _ref_binary("akmj,njk->anm", as_f64(d["in0"]), as_f64(d["in1"]))
+    assert _oracle.rel_err(out, d["out"]) <= 1e-12
