@@ -234,3 +234,20 @@ def test_error_codes():
     assert cabi.lib().eir_contract(None, None, None, None, None, None) == 52
     plan = cabi.ContractPlan(dims, cabi.FP32, cabi.FP32, cabi.FP32)
     assert plan.num_ops == 2 * 4 * 4 * 4 - 4 * 4  # ZERO first touch (BinaryContraction.cpp:459-462)
+
+
+def test_direct_kernel_division_by_multiplication():
+    """the direct CUDA-core kernel splits an index x < 2^32 by a dim size d
+    as q = (x * M) >> 64 with M = UINT64_MAX // d + 1 = ceil(2^64 / d) (the
+    planner's magic_of); exact for every such x and 2 <= d < 2^32 (Lemire,
+    Kaser, Kurz 2019). Checked on the edges of every multiple it can miss"""
+    rng = random.Random(7)
+    divisors = list(range(2, 300)) + [2 ** k for k in range(1, 32)] + [2 ** k - 1 for k in range(2, 33)] + \
+        [rng.randrange(2, 2 ** 32) for _ in range(300)]
+    for d in divisors:
+        m = (2 ** 64 - 1) // d + 1
+        qs = {0, 1, 2, (2 ** 32 - 1) // d} | {rng.randrange(0, (2 ** 32 - 1) // d + 1) for _ in range(20)}
+        for q in qs:
+            for x in (q * d - 1, q * d, q * d + d - 1):
+                if 0 <= x < 2 ** 32:
+                    assert (x * m) >> 64 == x // d, (x, d)
